@@ -1,0 +1,130 @@
+/*
+ * paraconv2d.h -- C ABI of the B200 (sm_100a) ParaConv2d paraboloid convolution.
+ *
+ * libpc2d_sm100.so exports these entry points.  The signatures use only plain
+ * C types: device pointers, sizes, a CUDA stream passed as void*.  They do not
+ * use torch types.  The torch op library libptparaconv2d.so (schema
+ * ptparaconv2d::forward / ptparaconv2d::backward, identical to the reference)
+ * is a thin client of this ABI.
+ *
+ * Semantics follow the reference op GeoND-tech/ParaConv2d:
+ *   input   [n][channels][height][width], already padded by the caller
+ *   pars    [h0 (m) | h (m*d) | p (m*d) | p0 (m)], d = channels*k0*k1,
+ *           h and p row-major [m][channels][k0][k1]   (paraconv2d.cc:23-37)
+ *   output, hsum  [n][m][out_height][out_width]
+ *   out_height = (height - dl0*(k0-1) - 1)/s0 + 1     (paraconv2d.cc:268-269)
+ *   hsum   = h0[j] + sum_k h[j,k] * win[k]
+ *   output = f * (hsum^2 - sum_k (win[k] - p[j,k])^2 - p0[j]^2)
+ * The window is flipped: tap (ix2, iy2) reads input row
+ * oy*s0 + (k0-1-ix2)*dl0 and column ox*s1 + (k1-1-iy2)*dl1 (paraconv2d.cc:89-92).
+ * The backward pass returns inputgrad [n][channels][height][width] (scaled by
+ * 2, with no output factor, paraconv2d.cc:166-183) and parsgrad, packed like
+ * pars (scaled by 2f, paraconv2d.cc:226-237).  When skip_input_grad is
+ * nonzero, inputgrad is written as all zeros (paraconv2d.cc:147,153).
+ *
+ * Conventions of every compute entry point:
+ *   - all tensor pointers are device pointers to contiguous arrays of the
+ *     given dtype; inputs are read only; outputs are fully overwritten;
+ *   - work is enqueued on `stream` (a cudaStream_t; NULL = legacy default);
+ *     nothing synchronises the host, and nothing allocates device memory:
+ *     scratch comes from the caller's `workspace` of at least the size
+ *     reported by the matching *_workspace_size query (256-byte aligned);
+ *   - the return value is a pc2d_status; on failure pc2d_last_error()
+ *     gives a message (thread local).  Odd kernel sizes only: even sizes make
+ *     the reference read outside the window and are rejected.
+ *   - kernels that wait on on-chip barriers give up after a bounded number of
+ *     polls; they then record PC2D_ERR_TIMEOUT in a device-side flag that
+ *     pc2d_device_status() reads (it synchronises the device).
+ */
+#ifndef PARACONV2D_B200_H_
+#define PARACONV2D_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PC2D_ABI_VERSION 1
+
+typedef enum {
+  PC2D_OK = 0,
+  PC2D_ERR_INVALID_ARGUMENT = 1, /* bad shape, dtype, null pointer, pars length ... */
+  PC2D_ERR_UNSUPPORTED = 2,      /* valid for the reference but not supported here */
+  PC2D_ERR_WORKSPACE = 3,        /* workspace missing, too small or misaligned */
+  PC2D_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed */
+  PC2D_ERR_TIMEOUT = 5           /* a device-side barrier wait gave up */
+} pc2d_status;
+
+typedef enum { PC2D_DTYPE_F32 = 0, PC2D_DTYPE_F64 = 1 } pc2d_dtype;
+
+/* Kernel families.  AUTO picks the tcgen05 tensor-core kernels (3xTF32 split
+ * precision) for fp32 shapes they support and the CUDA-core kernels
+ * otherwise; SIMT forces the CUDA-core kernels (fp32 or fp64 FMA). */
+typedef enum { PC2D_ALGO_AUTO = 0, PC2D_ALGO_SIMT = 1, PC2D_ALGO_TC = 2 } pc2d_algo;
+
+/* Library ABI version (PC2D_ABI_VERSION). */
+int pc2d_abi_version(void);
+
+/* Output extent along one axis (reference paraconv2d.cc:268-269); <= 0 means empty/invalid. */
+int pc2d_out_size(int in, int kernel, int stride, int dilation);
+
+/* Number of output channels implied by the flat parameter count
+ * (reference paraconv2d.cc:266: m = npars / (2*(d+1))); -1 when npars is not
+ * a positive multiple of 2*(d+1). */
+int64_t pc2d_infer_m(int64_t npars, int channels, int k0, int k1);
+
+/* Process-wide kernel family selection (default PC2D_ALGO_AUTO).  Returns the previous value. */
+int pc2d_set_algo(int algo);
+int pc2d_get_algo(void);
+
+/* Scratch bytes pc2d_forward needs for this problem (0 is possible). */
+size_t pc2d_forward_workspace_size(int dtype, int n, int channels, int height, int width, int m,
+                                   int k0, int k1, int s0, int s1, int dl0, int dl1);
+
+/* Forward pass.  Replaces the reference's paraconv2d_forward_cuda_main<T>
+ * (paraconv2d.cu:81-123) and the kernels it launches
+ * (paraconv2dkernels.cu:27-141); `factor` is the op's `doublefactor`
+ * argument (paraconv2d.cc:292). */
+int pc2d_forward(int dtype, const void *input, const void *pars, double factor,
+                 int k0, int k1, int s0, int s1, int dl0, int dl1,
+                 int n, int channels, int height, int width, int m,
+                 void *output, void *hsum, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Scratch bytes pc2d_backward needs for this problem. */
+size_t pc2d_backward_workspace_size(int dtype, int n, int channels, int height, int width, int m,
+                                    int k0, int k1, int s0, int s1, int dl0, int dl1,
+                                    int skip_input_grad);
+
+/* Backward pass.  Replaces the reference's paraconv2d_backward_cuda_main<T>
+ * (paraconv2d.cu:131-223) and the kernels it launches
+ * (paraconv2dgradkernels.cu:27-249). */
+int pc2d_backward(int dtype, const void *grad, const void *input, const void *pars, const void *hsum,
+                  double factor, int k0, int k1, int s0, int s1, int dl0, int dl1,
+                  int n, int channels, int height, int width, int m, int skip_input_grad,
+                  void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Human-readable name of a pc2d_status. */
+const char *pc2d_status_string(int status);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char *pc2d_last_error(void);
+
+/* Synchronises the current device and returns PC2D_OK, or the first
+ * device-side error (PC2D_ERR_TIMEOUT) recorded since the last call to
+ * pc2d_clear_device_status(); also reports pending CUDA errors as PC2D_ERR_CUDA. */
+int pc2d_device_status(void);
+int pc2d_clear_device_status(void);
+
+/* Test hook: a kernel that waits on an mbarrier that nothing completes, with
+ * a wait limit of `max_polls`; it must return by itself and record
+ * PC2D_ERR_TIMEOUT.  Used to check the bounded-wait path without faulting or
+ * hanging the GPU. */
+int pc2d_selftest_bounded_wait(unsigned int max_polls, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PARACONV2D_B200_H_ */

@@ -1,0 +1,92 @@
+// Shared definitions of the ParaConv2d sm_100a kernels: the problem
+// descriptor, launch helpers and the device-side error flag.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "paraconv2d.h"
+
+namespace pc2d {
+
+// One ParaConv2d problem (a padded input batch and one parameter vector).
+// Field names follow the reference op (paraconv2d.cc:254-269).
+struct Problem {
+  int n, C, H, W;         // padded input [n][C][H][W]
+  int m;                  // output channels
+  int k0, k1, s0, s1, dl0, dl1;
+  int P, Q;               // output extent
+  int T;                  // taps per channel, k0*k1
+  int64_t d;              // C*T, length of one window
+  int64_t HW, PQ, CHW, NPQ, NHW;
+};
+
+inline Problem make_problem(int n, int C, int H, int W, int m, int k0, int k1, int s0, int s1,
+                            int dl0, int dl1) {
+  Problem p;
+  p.n = n; p.C = C; p.H = H; p.W = W; p.m = m;
+  p.k0 = k0; p.k1 = k1; p.s0 = s0; p.s1 = s1; p.dl0 = dl0; p.dl1 = dl1;
+  p.P = (s0 > 0) ? ((H - dl0 * (k0 - 1) - 1) / s0) + 1 : 0;
+  p.Q = (s1 > 0) ? ((W - dl1 * (k1 - 1) - 1) / s1) + 1 : 0;
+  p.T = k0 * k1;
+  p.d = (int64_t)C * p.T;
+  p.HW = (int64_t)H * W;
+  p.PQ = (int64_t)p.P * p.Q;
+  p.CHW = (int64_t)C * p.HW;
+  p.NPQ = (int64_t)n * p.PQ;
+  p.NHW = (int64_t)n * p.HW;
+  return p;
+}
+
+// Offset, within one input channel plane, of tap `tap` (= ix2*k1 + iy2) of the
+// window of output pixel (0,0).  The window is flipped: tap (ix2, iy2) reads
+// row (k0-1-ix2)*dl0 and column (k1-1-iy2)*dl1 (reference paraconv2d.cc:89-92,
+// with 2*(k/2) = k-1 for the odd kernel sizes accepted here).
+__host__ __device__ inline int tap_row(const Problem &p, int tap) { return (p.k0 - 1 - tap / p.k1) * p.dl0; }
+__host__ __device__ inline int tap_col(const Problem &p, int tap) { return (p.k1 - 1 - tap % p.k1) * p.dl1; }
+
+inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Device-side status word of the current device: the first nonzero
+// pc2d_status a kernel records (a bounded mbarrier wait that gave up).  It is
+// a __device__ variable of the ABI translation unit; kernels get its address
+// as an argument.  Read by pc2d_device_status().
+int *device_status_ptr();
+
+__device__ __forceinline__ void record_device_error(int *status, int code) { atomicCAS(status, 0, code); }
+
+// Host-side error message of the last failing ABI call on this thread.
+void set_last_error(const char *fmt, ...);
+
+// Launchers implemented by the kernel translation units.
+template <typename T>
+int simt_forward(const Problem &p, const T *x, const T *pars, double factor, T *out, T *hsum,
+                 cudaStream_t stream);
+template <typename T>
+size_t simt_backward_workspace(const Problem &p, bool skip_input_grad);
+template <typename T>
+int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, const T *hsum,
+                  double factor, bool skip_input_grad, T *dx, T *dpars, void *ws, size_t ws_bytes,
+                  cudaStream_t stream);
+
+}  // namespace pc2d
+
+#define PC2D_CUDA_CHECK(call)                                                          \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess) {                                                           \
+      pc2d::set_last_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_),      \
+                           __FILE__, __LINE__);                                         \
+      return PC2D_ERR_CUDA;                                                            \
+    }                                                                                  \
+  } while (0)
+
+#define PC2D_LAUNCH_CHECK(what)                                                        \
+  do {                                                                                 \
+    cudaError_t e_ = cudaGetLastError();                                               \
+    if (e_ != cudaSuccess) {                                                           \
+      pc2d::set_last_error("launch of %s failed: %s", what, cudaGetErrorString(e_));   \
+      return PC2D_ERR_CUDA;                                                            \
+    }                                                                                  \
+  } while (0)

@@ -1,0 +1,27 @@
+// Host entry points of the tcgen05 (tensor-core, 3xTF32) kernels.
+#pragma once
+
+#include "pc2d_common.cuh"
+
+namespace pc2d {
+
+// Forward pass (pc2d_tc_fwd.cu).
+bool tc_forward_supported(const Problem &p);
+size_t tc_forward_workspace(const Problem &p);
+int tc_forward(const Problem &p, const float *x, const float *pars, double factor, float *out, float *hsum,
+               void *ws, cudaStream_t stream);
+
+// Backward pass (pc2d_tc_bwd.cu).
+bool tc_backward_supported(const Problem &p);
+size_t tc_backward_workspace(const Problem &p, bool skip_input_grad);
+int tc_backward(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum,
+                double factor, bool skip_input_grad, float *dx, float *dpars, void *ws, size_t ws_bytes,
+                cudaStream_t stream);
+
+// A kernel that waits on an mbarrier nothing completes, bounded by timeout_us.
+int tc_selftest_bounded_wait(unsigned int timeout_us, int *status, cudaStream_t stream);
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+}  // namespace pc2d

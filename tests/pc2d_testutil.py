@@ -1,0 +1,120 @@
+"""Shared helpers of the test suite: golden fixtures, tolerance policy and a
+float64 torch restatement of the op used as a second reference at sizes the
+CPU oracle cannot reach quickly.
+
+Tolerance policy (per tensor, against the fp32 oracle = the reference CPU op):
+  output, hsum                elementwise |a - b| <= 1e-5 + 1e-4 |b|
+  inputgrad, h0/h/p/p0 grads  max |a - b| <= 1e-4 * max |b|
+The gradients are long reductions whose fp32 value depends on summation
+order; the reference's own fp32 result is not elementwise within 1e-5/1e-4 of
+the exact (fp64) value, so no other summation order can be.  Where an fp64
+reference is available the tests also require that our max error against it
+is no worse than twice the fp32 oracle's own.
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+OUT_ATOL, OUT_RTOL = 1e-5, 1e-4
+GRAD_REL = 1e-4
+
+
+def golden_manifest():
+    with open(os.path.join(GOLDEN, "manifest.json")) as f:
+        return json.load(f)
+
+
+def load_golden(name):
+    meta = golden_manifest()[name]
+    with np.load(os.path.join(GOLDEN, f"{name}.npz")) as z:
+        arrays = {k: z[k] for k in z.files}
+    return arrays, meta
+
+
+def elementwise_excess(a, b, atol=OUT_ATOL, rtol=OUT_RTOL):
+    """max over elements of |a-b| / (atol + rtol |b|); <= 1 passes."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    if a.size == 0:
+        return 0.0
+    return float(np.max(np.abs(a - b) / (atol + rtol * np.abs(b))))
+
+
+def maxrel_excess(a, b, rel=GRAD_REL):
+    """max |a-b| / (rel * max |b|); <= 1 passes."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    if a.size == 0:
+        return 0.0
+    scale = float(np.max(np.abs(b)))
+    err = float(np.max(np.abs(a - b)))
+    if scale == 0.0:
+        return 0.0 if err == 0.0 else float("inf")
+    return err / (rel * scale)
+
+
+def split_pars(pars, m, d):
+    pars = np.asarray(pars)
+    return pars[:m], pars[m:m + m * d], pars[m + m * d:m + 2 * m * d], pars[m + 2 * m * d:]
+
+
+def check_outputs(out, hsum, ref_out, ref_hsum):
+    e_out = elementwise_excess(out, ref_out)
+    e_hs = elementwise_excess(hsum, ref_hsum)
+    assert e_out <= 1.0, f"output exceeds 1e-5/1e-4 elementwise by {e_out:.3g}x"
+    assert e_hs <= 1.0, f"hsum exceeds 1e-5/1e-4 elementwise by {e_hs:.3g}x"
+    return e_out, e_hs
+
+
+def check_grads(dx, dpars, ref_dx, ref_dpars, m, d, skip_input_grad=False):
+    res = {}
+    if skip_input_grad:
+        assert np.all(np.asarray(dx) == 0), "inputgrad must be all zero when skip_input_grad"
+        res["dx"] = 0.0
+    else:
+        res["dx"] = maxrel_excess(dx, ref_dx)
+    for name, a, b in zip(("dh0", "dh", "dp", "dp0"), split_pars(dpars, m, d), split_pars(ref_dpars, m, d)):
+        res[name] = maxrel_excess(a, b)
+    bad = {k: v for k, v in res.items() if v > 1.0}
+    assert not bad, f"gradients exceed max|a-b| <= 1e-4 max|b|: {bad}"
+    return res
+
+
+# --------------------------------------------------------------------------
+# float64 torch restatement (test reference for large sizes)
+# --------------------------------------------------------------------------
+
+def torch_reference(x, pars, factor, k, s, dl, grad=None, skip_input_grad=False):
+    """Forward (and, with `grad`, backward) of the op in float64 torch, from
+    the conv decomposition: hsum = h0 + conv(x, flip(h)), |win - p|^2 =
+    conv(x^2, 1) - 2 conv(x, flip(p)) + |p|^2.  Returns numpy arrays
+    (out, hsum[, dx, dpars]) with dx in the op's convention (2 * scatter, no
+    output factor) and dpars packed like pars."""
+    k0, k1 = k
+    x = torch.as_tensor(x).to(torch.float64).clone().requires_grad_(grad is not None)
+    pars = torch.as_tensor(pars).to(x.device, torch.float64).clone().requires_grad_(grad is not None)
+    C = x.shape[1]
+    d = C * k0 * k1
+    m = pars.numel() // (2 * (d + 1))
+    h0, h, p, p0 = pars[:m], pars[m:m + m * d], pars[m + m * d:m + 2 * m * d], pars[m + 2 * m * d:]
+    H = h.reshape(m, C, k0, k1).flip(2, 3)
+    Pw = p.reshape(m, C, k0, k1).flip(2, 3)
+    ones = torch.ones(1, C, k0, k1, dtype=torch.float64, device=x.device)
+    hs = F.conv2d(x, H, stride=s, dilation=dl) + h0.view(1, m, 1, 1)
+    px = F.conv2d(x, Pw, stride=s, dilation=dl)
+    s2 = F.conv2d(x * x, ones, stride=s, dilation=dl)
+    pp = (p.reshape(m, d) ** 2).sum(1).view(1, m, 1, 1)
+    out = factor * (hs * hs - (s2 - 2 * px + pp) - (p0 * p0).view(1, m, 1, 1))
+    if grad is None:
+        return out.detach().cpu().numpy(), hs.detach().cpu().numpy()
+    g = torch.as_tensor(grad).to(x.device, torch.float64)
+    dx, dpars = torch.autograd.grad(out, (x, pars), g)
+    dx = torch.zeros_like(dx) if skip_input_grad else dx / factor
+    return (out.detach().cpu().numpy(), hs.detach().cpu().numpy(), dx.cpu().numpy(), dpars.cpu().numpy())

@@ -1,0 +1,168 @@
+"""Parity of the CUDA kernels with the reference CPU op, through the C ABI.
+
+Reference values come from the golden fixtures (produced by the reference
+op itself) and from the oracle (the C restatement pinned bit-for-bit to the
+reference) on seeded subsets of the measured workloads.  Tolerances: see
+pc2d_testutil (output/hsum elementwise 1e-5 + 1e-4|b|; gradients
+max|a-b| <= 1e-4 max|b|).  Both kernel families are checked: AUTO (tcgen05
+3xTF32 kernels where they apply) and SIMT (CUDA-core FMA).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from cabi_runner import algo, backward, forward
+from paraconv2d_b200 import PC2D_ALGO_AUTO, PC2D_ALGO_SIMT, _lib, workloads
+from pc2d_testutil import (check_grads, check_outputs, elementwise_excess, golden_manifest, load_golden,
+                           maxrel_excess, torch_reference)
+
+pytestmark = pytest.mark.gpu
+
+ALGOS = {"auto": PC2D_ALGO_AUTO, "simt": PC2D_ALGO_SIMT}
+NAMES = sorted(golden_manifest())
+
+
+def _cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("algo_name", sorted(ALGOS))
+@pytest.mark.parametrize("name", NAMES)
+def test_golden(name, algo_name):
+    a, meta = load_golden(name)
+    k, s, dl, f = meta["kernel_size"], meta["stride"], meta["dilation"], meta["factor"]
+    C = meta["C"]
+    d = C * k[0] * k[1]
+    with algo(ALGOS[algo_name]):
+        x, pars = _cuda(a["x"]), _cuda(a["pars"])
+        out, hsum = forward(x, pars, f, k, s, dl)
+        dx, dpars = backward(_cuda(a["grad"]), x, pars, _cuda(a["hsum"]), f, k, s, dl, meta["skip_input_grad"])
+        torch.cuda.synchronize()
+    check_outputs(out.cpu().numpy(), hsum.cpu().numpy(), a["out"], a["hsum"])
+    check_grads(dx.cpu().numpy(), dpars.cpu().numpy(), a["dx"], a["dpars"], meta["m"], d, meta["skip_input_grad"])
+
+
+def _subset_case(name, n):
+    wl = workloads.WORKLOADS[name]
+    L = wl.layer
+    x, pars, g = workloads.draw(wl, n=n)
+    grad = workloads.draw_grad(wl, g, n=n)
+    xp = workloads.pad_input(x, L.p)
+    return wl, L, xp.numpy(), pars[0].numpy(), grad.numpy()
+
+
+@pytest.mark.parametrize("algo_name", sorted(ALGOS))
+@pytest.mark.parametrize("name,n", [("c1", 2), ("c2", 2), ("c3", 1), ("c4", 1)])
+def test_workload_subset_vs_oracle(name, n, algo_name):
+    """The first n images of each measured workload against the oracle."""
+    wl, L, xp, pars, grad = _subset_case(name, n)
+    ref_out, ref_hs = oracle.forward(xp, pars, 1.0, L.k, L.s, 1)
+    ref_dx, ref_dp = oracle.backward(grad, xp, pars, ref_hs, 1.0, L.k, L.s, 1, False)
+    d = L.cin * L.k * L.k
+    with algo(ALGOS[algo_name]):
+        x, p = _cuda(xp), _cuda(pars)
+        out, hsum = forward(x, p, 1.0, L.k, L.s, 1)
+        dx, dp = backward(_cuda(grad), x, p, _cuda(ref_hs), 1.0, L.k, L.s, 1)
+        torch.cuda.synchronize()
+    check_outputs(out.cpu().numpy(), hsum.cpu().numpy(), ref_out, ref_hs)
+    check_grads(dx.cpu().numpy(), dp.cpu().numpy(), ref_dx, ref_dp, L.cout, d)
+
+
+@pytest.mark.parametrize("name", ["c2", "c3", "c4"])
+def test_full_size_forward_vs_float64(name):
+    """Full-size forward of each measured workload against the float64 torch
+    restatement: same elementwise tolerance as against the oracle."""
+    wl = workloads.WORKLOADS[name]
+    L = wl.layer
+    x, pars, g = workloads.draw(wl)
+    xp = workloads.pad_input(x, L.p).cuda()
+    p = pars[0].cuda()
+    out, hsum = forward(xp, p, 1.0, L.k, L.s, 1)
+    ref_out, ref_hs = torch_reference(xp, p, 1.0, (L.k, L.k), L.s, 1)
+    torch.cuda.synchronize()
+    assert elementwise_excess(out.cpu().numpy(), ref_out) <= 1.0
+    assert elementwise_excess(hsum.cpu().numpy(), ref_hs) <= 1.0
+
+
+def test_full_size_backward_c2_vs_float64():
+    """Full-size c2 backward: gradients against the float64 torch restatement,
+    max|a-b| <= 1e-4 max|b|, and batch additivity (grads of the full batch =
+    sum over two halves)."""
+    wl = workloads.WORKLOADS["c2"]
+    L = wl.layer
+    x, pars, g = workloads.draw(wl)
+    grad = workloads.draw_grad(wl, g).cuda()
+    xp = workloads.pad_input(x, L.p).cuda()
+    p = pars[0].cuda()
+    out, hsum = forward(xp, p, 1.0, L.k, L.s, 1)
+    dx, dp = backward(grad, xp, p, hsum, 1.0, L.k, L.s, 1)
+    _, _, rdx, rdp = torch_reference(xp, p, 1.0, (L.k, L.k), L.s, 1, grad=grad)
+    assert maxrel_excess(dx.cpu().numpy(), rdx) <= 1.0
+    d = L.cin * L.k * L.k
+    check_grads(dx.cpu().numpy(), dp.cpu().numpy(), rdx, rdp, L.cout, d)
+    h = wl.n // 2
+    dpa = backward(grad[:h].contiguous(), xp[:h].contiguous(), p, hsum[:h].contiguous(), 1.0, L.k, L.s, 1)[1]
+    dpb = backward(grad[h:].contiguous(), xp[h:].contiguous(), p, hsum[h:].contiguous(), 1.0, L.k, L.s, 1)[1]
+    assert maxrel_excess((dpa + dpb).cpu().numpy(), dp.cpu().numpy()) <= 1.0
+
+
+@pytest.mark.parametrize("algo_name", sorted(ALGOS))
+def test_deterministic(algo_name):
+    """No floating-point atomics: two runs are bitwise identical."""
+    wl, L, xp, pars, grad = _subset_case("c2", 4)
+    with algo(ALGOS[algo_name]):
+        x, p, g = _cuda(xp), _cuda(pars), _cuda(grad)
+        r1 = forward(x, p, 1.0, L.k, L.s, 1)
+        r2 = forward(x, p, 1.0, L.k, L.s, 1)
+        b1 = backward(g, x, p, r1[1], 1.0, L.k, L.s, 1)
+        b2 = backward(g, x, p, r1[1], 1.0, L.k, L.s, 1)
+    for u, v in zip(r1 + b1, r2 + b2):
+        assert torch.equal(u, v)
+
+
+def test_forward_batch_independent():
+    """Each image's output does not depend on the rest of the batch (bitwise)."""
+    wl, L, xp, pars, grad = _subset_case("c2", 3)
+    x, p = _cuda(xp), _cuda(pars)
+    full = forward(x, p, 1.0, L.k, L.s, 1)
+    one = forward(x[1:2].contiguous(), p, 1.0, L.k, L.s, 1)
+    assert torch.equal(full[0][1:2], one[0]) and torch.equal(full[1][1:2], one[1])
+
+
+def test_tc_and_simt_agree():
+    """The two kernel families agree to well within the tolerance."""
+    wl, L, xp, pars, grad = _subset_case("c3", 1)
+    x, p = _cuda(xp), _cuda(pars)
+    with algo(PC2D_ALGO_AUTO):
+        a = forward(x, p, 1.0, L.k, L.s, 1)
+    with algo(PC2D_ALGO_SIMT):
+        b = forward(x, p, 1.0, L.k, L.s, 1)
+    assert elementwise_excess(a[0].cpu().numpy(), b[0].cpu().numpy()) <= 0.5
+    assert elementwise_excess(a[1].cpu().numpy(), b[1].cpu().numpy()) <= 0.5
+
+
+def test_edge_empty_batch_and_m1():
+    x = torch.zeros((0, 3, 8, 8), device="cuda")
+    pars = torch.randn(2 * 1 * (27 + 1), device="cuda")
+    out, hs = forward(x, pars, 1.0, 3, 1, 1)
+    assert out.shape == (0, 1, 6, 6)
+    dx, dp = backward(torch.zeros_like(out), x, pars, hs, 1.0, 3, 1, 1)
+    assert dx.shape == x.shape and torch.count_nonzero(dp) == 0
+
+
+def test_bounded_wait_selftest():
+    """A device-side wait on a barrier nothing completes returns by itself
+    and records PC2D_ERR_TIMEOUT; the context stays usable."""
+    lib = _lib.cabi()
+    assert lib.pc2d_clear_device_status() == 0
+    assert lib.pc2d_selftest_bounded_wait(200000, None) == 0
+    assert lib.pc2d_device_status() == _lib.PC2D_ERR_TIMEOUT
+    assert lib.pc2d_clear_device_status() == 0
+    assert lib.pc2d_device_status() == 0
+    y = torch.ones(4, device="cuda") * 2
+    assert float(y.sum()) == 8.0
+
+
+def test_no_device_errors_after_suite():
+    assert _lib.cabi().pc2d_device_status() == 0
