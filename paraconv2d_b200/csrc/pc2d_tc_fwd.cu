@@ -6,76 +6,76 @@
 //   hsum = h0[j] + H[j].win
 //   out  = f * (hsum^2 - S2[i] + 2 P[j].win - |P[j]|^2 - p0[j]^2),
 //   S2[i] = sum_k win[k]^2
-// so H.win and P.win form one implicit GEMM with M = 128 output pixels per
-// tile, N = NB output channels per channel block (NB <= 64) for each of H and
-// P, and K = the window (C*k0*k1), swept 16 at a time.
+// so H.win and P.win form one implicit GEMM: M = 128 consecutive output
+// pixels of one image per tile, N = [H;P] rows of a channel block (2*NB,
+// NB <= 64) and K = the window (C*k0*k1), swept 32 at a time.
 //
-// Operands:
-//   A (the im2col window, M x K) lives in Tensor Memory.  Four producer
-//     warps (one TMEM lane = one output pixel per thread) gather the window
-//     with 4-byte cp.async copies (coalesced across the 32 pixels of a warp)
-//     into a per-thread shared-memory ring that keeps 5 stages of 16 K in
-//     flight, then split every value into tf32 hi + lo, accumulate S2, and
-//     tcgen05.st the hi and lo slices into a 4-stage ring of TMEM columns.
-//   B ([H;P], 2NB x K) is split into hi/lo once per call by a prep kernel,
-//     already in the 128-byte-swizzled K-major layout, and streamed into a
-//     4-stage shared-memory ring (32 K per stage) by 1-D bulk async copies.
+// Data movement per 32-K stage (3 stages in flight):
+//   - the loader warp issues 1-D bulk copies of (a) the pre-split weights of
+//     the stage ([H;P] hi and lo, 128-byte-swizzled K-major, written once per
+//     call by a prep kernel) and (b) the input "halo" of the stage: for each
+//     channel the stage's window touches, the contiguous run of input rows
+//     the tile reads (16-byte rounded), all completing on one barrier;
+//   - four producer warps (one TMEM lane = one output pixel per thread)
+//     gather the 32 window values of their pixel from the halo in shared
+//     memory, split them into tf32 hi + lo, accumulate S2, and tcgen05.st
+//     the hi and lo slices into the stage's TMEM columns (A operand);
+//   - one thread of the MMA warp issues, per 8-wide K step, the three
+//     products Ahi*Bhi + Alo*Bhi + Ahi*Blo as MMAs with N = 2NB.
 //
-// Accumulation (3xTF32 = Ahi*Bhi + Alo*Bhi + Ahi*Blo per 8-wide K step,
-// each one MMA of N = 2NB over [H;P]):
-//   The tensor core's fp32 accumulation loses up to one unit in the last
-//   place of the accumulator per instruction, so a long K sweep into one
-//   accumulator drifts by O(K/8) ulps of the running sum.  Instead, every 32
-//   K of the sweep accumulate into a fresh partial sum (enable_input_d = 0)
-//   in one of three [H | P] slots of TMEM, and the epilogue warps drain each
-//   partial into fp32 registers (round-to-nearest adds) while the MMAs fill
-//   the next slot.  TMEM columns: slots [0,128) [128,256) [256,384); A
-//   stages [384,512) as 4 x (hi 16 | lo 16).
+// Accumulation: the tensor core's fp32 accumulation loses up to one unit in
+// the last place per instruction, so a long K sweep into one accumulator
+// drifts by O(K/8) ulps of the running sum.  Every 64 K therefore start a
+// fresh partial sum (enable_input_d = 0) in one of two [H | P] slots of TMEM,
+// and the epilogue warps drain each partial into fp32 registers
+// (round-to-nearest adds) while the MMAs fill the other slot.
+//   TMEM columns: slots [0,128) [128,256); A stages [256,448) as
+//   3 x (hi 32 | lo 32).
 //
 // Warp roles (320 threads, one CTA per SM, persistent over work items):
-//   warps 0-3 producers, warps 4-7 epilogue, warp 8 MMA issuer (and TMEM
-//   owner), warp 9 B loader.  Every barrier wait is bounded in
-//   time; a wait that gives up records PC2D_ERR_TIMEOUT, raises a CTA-wide
-//   abort flag, and the CTA drains its in-flight copies and MMAs and exits.
+//   warps 0-3 producers, 4-7 epilogue, 8 MMA issuer (and TMEM owner),
+//   9 loader.  Every barrier wait is bounded in time; a wait that gives up
+//   records PC2D_ERR_TIMEOUT, raises a CTA-wide abort flag, and the CTA
+//   drains its in-flight copies and MMAs and exits.
 #include <algorithm>
 #include <mutex>
 
-#include "pc2d_sm100.cuh"
 #include "pc2d_tc.cuh"
+#include "pc2d_tc_common.cuh"
 
 namespace pc2d {
 
 namespace {
 using namespace sm100;
+using tc::warp_wait;
+using tc::kWaitNs;
 
 constexpr int kTileM = 128;
-constexpr int kKB = 32;          // K per B stage (one 128-byte swizzle row of tf32)
-constexpr int kKA = 32;          // K per A stage (= one B stage)
-constexpr int kAStages = 2;
-constexpr int kBStages = 4;
+constexpr int kKS = 32;          // K per stage (one 128-byte swizzle row of tf32)
+constexpr int kMaxStages = 4;    // stages in flight (4, or 3 when shared memory is short)
+constexpr int kSlots = 2;        // partial-sum slots in TMEM
+constexpr int kGroupStages = 2;  // stages per partial sum (64 K)
 constexpr int kMaxNB = 64;
 constexpr int kMaxD = 8192;
-constexpr int kGroupStages = 1;  // A stages per partial sum (32 K)
-constexpr int kSlots = 3;        // partial-sum slots in TMEM
-constexpr int kDepth = 2;        // A stages whose window gathers are in flight (cp.async)
-constexpr int kRing = kDepth + 1;
 constexpr int kFwdThreads = 320;
-constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr int kMinSmem = 120 * 1024;  // keeps one CTA per SM (it owns all 512 TMEM columns)
-
-// TMEM column map: partial-sum slots [H | P] at 128 * slot (slots 0-2),
-// A stages at 384 + 64 * stage (hi 32 columns, then lo 32 columns).
-constexpr uint32_t kColA = 384;
+constexpr int kSmemLimit = 227 * 1024;
+constexpr uint32_t kColA = 256;       // A stages at 256 + 64 * stage: hi 32, lo 32
 
 struct FwdCfg {
-  int ncb;         // channel blocks
-  int NB;          // channels per block (multiple of 16, <= 64)
-  int N;           // rows of a B stage = 2*NB ([H;P])
-  int nKB;         // 32-wide K chunks (B stages per tile)
-  int nKA;         // A stages per tile (= nKB)
-  int nGroups;     // H partial sums per tile
-  int64_t tiles;   // 128-pixel tiles
-  int64_t items;   // tiles * ncb
+  int ncb;          // channel blocks
+  int NB;           // channels per block (multiple of 16, <= 64)
+  int N;            // rows of a B stage = 2*NB ([H;P])
+  int nK;           // 32-wide K stages per tile
+  int nst;          // stages in flight
+  int nGroups;      // partial sums per tile
+  int tpi;          // tiles per image
+  int64_t tiles;    // 128-pixel tiles (never crossing an image)
+  int64_t items;    // tiles * ncb
+  int PS;           // halo plane stride in floats (multiple of 4)
+  int nchs;         // channels a stage touches at most (<= 32)
+  uint32_t bstage;  // B bytes per stage (hi + lo)
+  uint32_t sstage;  // shared bytes per stage (B + halo, multiple of 1024)
 };
 
 FwdCfg fwd_cfg(const Problem &p) {
@@ -84,20 +84,41 @@ FwdCfg fwd_cfg(const Problem &p) {
   const int nb = ceil_div(p.m, c.ncb);
   c.NB = (nb + 15) / 16 * 16;
   c.N = 2 * c.NB;
-  c.nKB = ceil_div(p.d, kKB);
-  c.nKA = c.nKB;
-  c.nGroups = ceil_div(c.nKA, kGroupStages);
-  c.tiles = (p.NPQ + kTileM - 1) / kTileM;
+  c.nK = ceil_div(p.d, kKS);
+  c.nGroups = ceil_div(c.nK, kGroupStages);
+  c.tpi = ceil_div(p.PQ, kTileM);
+  c.tiles = (int64_t)p.n * c.tpi;
   c.items = c.tiles * c.ncb;
+  // output rows a run of 128 consecutive pixels of one image can touch
+  const int orow = std::min<int64_t>(p.P, (p.Q + kTileM - 2) / p.Q + 1);
+  const int R = (orow - 1) * p.s0 + (p.k0 - 1) * p.dl0 + 1;
+  c.PS = (int)(((int64_t)R * p.W + 8 + 3) / 4 * 4);
+  c.nchs = 0;
+  for (int kq = 0; kq < c.nK; ++kq) {
+    const int clo = (int)(((int64_t)kq * kKS) / p.T);
+    const int chi = (int)(std::min<int64_t>((int64_t)kq * kKS + kKS - 1, p.d - 1) / p.T);
+    c.nchs = std::max(c.nchs, chi - clo + 1);
+  }
+  c.bstage = (uint32_t)(2 * c.N * 128);
+  const size_t hb = align_up((size_t)c.nchs * c.PS * 4, 1024);
+  c.sstage = (uint32_t)(c.bstage + hb);
+  c.nst = kMaxStages;
   return c;
 }
 
-inline size_t fwd_bsplit_bytes(const FwdCfg &c) { return (size_t)c.ncb * c.nKB * 2 * c.N * 128; }
-__host__ __device__ inline uint32_t fwd_bstage_bytes(const FwdCfg &c) { return (uint32_t)(2 * c.N * 128); }
-inline size_t fwd_smem_bytes(const FwdCfg &c) {
-  size_t s = 1024 + (size_t)kBStages * fwd_bstage_bytes(c) + (size_t)kRing * kKA * kTileM * 4 +
-             (size_t)c.nKB * kKB * 4 + 2 * kTileM * 4 + 32 * 8 + 64;
+inline size_t fwd_bsplit_bytes(const FwdCfg &c) { return (size_t)c.ncb * c.nK * c.bstage; }
+inline size_t fwd_smem_bytes(const Problem &p, const FwdCfg &c) {
+  size_t s = 1024 + (size_t)c.nst * c.sstage + (size_t)c.nK * kKS * 8 + (size_t)kMaxStages * kKS * 4 +
+             (size_t)kMaxStages * 32 * 4 + 2 * kTileM * 4 + 24 * 8 + 64;
+  (void)p;
   return std::max<size_t>(s, kMinSmem);
+}
+
+// Picks 4 stages when they fit in shared memory, else 3.
+inline FwdCfg fwd_cfg_fit(const Problem &p) {
+  FwdCfg c = fwd_cfg(p);
+  if (fwd_smem_bytes(p, c) > (size_t)kSmemLimit) c.nst = 3;
+  return c;
 }
 
 // Splits [H;P] of channel block cb into hi/lo tf32 halves in the swizzled
@@ -107,7 +128,7 @@ inline size_t fwd_smem_bytes(const FwdCfg &c) {
 // and K >= d are zero.
 __global__ void tc_fwd_prep_weights(const float *__restrict__ pars, Problem p, FwdCfg c, float *__restrict__ wsB) {
   const int kc = blockIdx.x, cb = blockIdx.y;
-  float *blk = wsB + ((int64_t)cb * c.nKB + kc) * 2 * c.N * 32;
+  float *blk = wsB + ((int64_t)cb * c.nK + kc) * 2 * c.N * 32;
   const float *h = pars + p.m;
   const float *pp = h + (int64_t)p.m * p.d;
   for (int e = threadIdx.x; e < c.N * 32; e += blockDim.x) {
@@ -151,27 +172,30 @@ __global__ void tc_fwd_prep_consts(const float *__restrict__ pars, Problem p, Fw
   }
 }
 
-// Warp-uniform bounded wait: every lane polls, the warp agrees on the result.
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-  const bool ok = mbar_wait(bar, parity, kWaitNs, abort_flag);
-  return __all_sync(0xffffffffu, ok);
-}
+// Geometry of a tile: image, first pixel, first input row and rows of its halo.
+struct TileGeo {
+  int64_t n;
+  int p0, ir0, rows;
+};
 
-// Input offset of the window origin of output pixel g (or -1 past the end).
-__device__ __forceinline__ int64_t pixel_base(const Problem &p, int64_t g) {
-  if (g >= p.NPQ) return -1;
-  const int64_t nn = g / p.PQ;
-  const int64_t rr = g - nn * p.PQ;
-  const int oy = (int)(rr / p.Q), ox = (int)(rr - (int64_t)oy * p.Q);
-  return nn * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
+__device__ __forceinline__ TileGeo tile_geo(const Problem &p, const FwdCfg &c, int64_t t) {
+  TileGeo g;
+  g.n = t / c.tpi;
+  g.p0 = (int)(t - g.n * c.tpi) * kTileM;
+  const int plast = min(g.p0 + kTileM - 1, (int)p.PQ - 1);
+  const int oya = g.p0 / p.Q, oyb = plast / p.Q;
+  g.ir0 = oya * p.s0;
+  g.rows = (oyb - oya) * p.s0 + (p.k0 - 1) * p.dl0 + 1;
+  return g;
 }
 
 struct Smem {
-  uint8_t *sB;
-  float *ring;   // [kRing][kKA][128] gathered window values of A stages in flight
-  int *koff;
-  float *s2buf;  // [tile buffer 2][128]
-  uint64_t *a_full, *a_empty, *b_full, *b_empty, *gr_full, *gr_empty, *s2_full, *s2_empty, *final_bar;
+  uint8_t *stage;   // nst x [B hi | B lo | halo planes]
+  int2 *koff;       // per K: (channel, tap offset row*W + col), channel -1 past d
+  int *offs;        // [stage][32] halo offset of each K of the stage (-1 = zero)
+  int *lead;        // [stage][32] floats before each halo plane's first element
+  float *s2buf;     // [tile buffer 2][128]
+  uint64_t *full, *a_full, *s_empty, *gr_full, *gr_empty, *s2_full, *s2_empty, *final_bar;
   uint32_t *tmem_holder;
   volatile int *abort_flag;
 };
@@ -184,42 +208,39 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const uint32_t bstage = fwd_bstage_bytes(c);
-  const int dpad = c.nKB * kKB;
   Smem S;
-  S.sB = base;
-  S.ring = reinterpret_cast<float *>(base + kBStages * bstage);
-  S.koff = reinterpret_cast<int *>(S.ring + kRing * kKA * kTileM);
-  S.s2buf = reinterpret_cast<float *>(S.koff + dpad);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(S.s2buf + 2 * kTileM);
-  S.a_full = bars;
-  S.a_empty = bars + 4;
-  S.b_full = bars + 8;
-  S.b_empty = bars + 12;
-  S.gr_full = bars + 16;
-  S.gr_empty = bars + 20;
-  S.s2_full = bars + 24;
-  S.s2_empty = bars + 26;
-  S.final_bar = bars + 28;
-  S.tmem_holder = reinterpret_cast<uint32_t *>(bars + 29);
+  const int nst = c.nst;
+  S.stage = base;
+  S.koff = reinterpret_cast<int2 *>(base + (size_t)nst * c.sstage);
+  S.offs = reinterpret_cast<int *>(S.koff + c.nK * kKS);
+  S.lead = S.offs + kMaxStages * kKS;
+  S.s2buf = reinterpret_cast<float *>(S.lead + kMaxStages * 32);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(
+      (reinterpret_cast<uintptr_t>(S.s2buf + 2 * kTileM) + 7) & ~(uintptr_t)7);
+  S.full = bars;            // [4] halo + B + offsets landed (loader expect_tx)
+  S.a_full = bars + 4;      // [4] A stage in TMEM (128 producer arrivals)
+  S.s_empty = bars + 8;     // [4] stage consumed by the MMAs (commit)
+  S.gr_full = bars + 12;    // [2] partial sum ready (commit)
+  S.gr_empty = bars + 14;   // [2] partial sum drained (128 epilogue arrivals)
+  S.s2_full = bars + 16;    // [2]
+  S.s2_empty = bars + 18;   // [2]
+  S.final_bar = bars + 20;
+  S.tmem_holder = reinterpret_cast<uint32_t *>(bars + 21);
   S.abort_flag = reinterpret_cast<volatile int *>(S.tmem_holder + 1);
 
-  // Per-K input offset of the flipped window relative to the window origin;
-  // -1 marks the zero padding of the last K chunk.
-  for (int k = threadIdx.x; k < dpad; k += blockDim.x) {
-    int v = -1;
+  for (int k = threadIdx.x; k < c.nK * kKS; k += blockDim.x) {
+    int2 v = make_int2(-1, 0);
     if (k < p.d) {
       const int ch = k / p.T, tap = k - ch * p.T;
-      v = (int)((int64_t)ch * p.HW + (int64_t)tap_row(p, tap) * p.W + tap_col(p, tap));
+      v = make_int2(ch, tap_row(p, tap) * p.W + tap_col(p, tap));
     }
     S.koff[k] = v;
   }
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kMaxStages; ++i) {
+      mbar_init(&S.full[i], 1);
       mbar_init(&S.a_full[i], 128);
-      mbar_init(&S.a_empty[i], 1);
-      mbar_init(&S.b_full[i], 1);
-      mbar_init(&S.b_empty[i], 1);
+      mbar_init(&S.s_empty[i], 1);
     }
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&S.gr_full[i], 1);
@@ -245,68 +266,58 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
 
   if (warp < 4) {
     // ---------------------------------------------------------- producers
-    const int r = warp * 32 + lane;      // pixel row of the tile = TMEM lane
+    const int r = warp * 32 + lane;  // pixel of the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    // Issue cursor: the next A stage whose window values are copied
-    // (cp.async, zero-filled outside the window) into ring slot s % kRing.
-    // Each thread copies and later reads only its own pixel's values.
-    int64_t i_item = blockIdx.x;
-    int i_kq = 0;
-    int64_t i_base = (i_item < c.items) ? pixel_base(p, (i_item / c.ncb) * kTileM + r) : -1;
-    auto issue = [&](uint32_t s_index) {
-      if (i_item < c.items) {
-        float *dst = S.ring + (s_index % kRing) * (kKA * kTileM) + r;
-#pragma unroll
-        for (int kk = 0; kk < kKA; ++kk) {
-          const int o = S.koff[i_kq * kKA + kk];
-          const bool v = (i_base >= 0 && o >= 0);
-          cp_async4(dst + kk * kTileM, x + (v ? i_base + o : 0), v);
-        }
-        if (++i_kq == c.nKA) {
-          i_kq = 0;
-          i_item += gridDim.x;
-          i_base = (i_item < c.items) ? pixel_base(p, (i_item / c.ncb) * kTileM + r) : -1;
-        }
-      }
-      cp_async_commit();
-    };
-#pragma unroll 1
-    for (int d0 = 0; d0 < kDepth; ++d0) issue(d0);
-    uint32_t s = 0;
+    uint32_t it = 0;
     int64_t li = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x, ++li) {
+      const TileGeo tg = tile_geo(p, c, item / c.ncb);
+      const int pix = tg.p0 + r;
+      const bool valid = pix < p.PQ;
+      int poff = 0;
+      if (valid) {
+        const int oy = pix / p.Q, ox = pix - (pix / p.Q) * p.Q;
+        poff = (oy * p.s0 - tg.ir0) * p.W + ox * p.s1;
+      }
       float s2 = 0.f;
-      for (int kq = 0; kq < c.nKA; ++kq, ++s) {
-        cp_async_wait<kDepth - 1>();
-        float cur[kKA];
-        const float *src = S.ring + (s % kRing) * (kKA * kTileM) + r;
-#pragma unroll
-        for (int kk = 0; kk < kKA; ++kk) cur[kk] = src[kk * kTileM];
-        uint32_t hi[kKA], lo[kKA];
-#pragma unroll
-        for (int kk = 0; kk < kKA; ++kk) {
-          s2 = fmaf(cur[kk], cur[kk], s2);
-          hi[kk] = tf32_hi_bits(cur[kk]);
-          lo[kk] = __float_as_uint(cur[kk] - __uint_as_float(hi[kk]));
-        }
-        issue(s + kDepth);
-        const uint32_t sa = s % kAStages, ph = (s / kAStages) & 1;
-        if (!warp_wait(&S.a_empty[sa], ph ^ 1, S.abort_flag)) {
+      for (int kq = 0; kq < c.nK; ++kq, ++it) {
+        const uint32_t st = it % nst, ph = (it / nst) & 1;
+        if (!warp_wait(&S.full[st], ph, S.abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t acol = tmem + lane_off + kColA + sa * 64;
+        const float *halo = reinterpret_cast<const float *>(S.stage + (size_t)st * c.sstage + c.bstage);
+        const int4 *offs = reinterpret_cast<const int4 *>(S.offs + st * kKS);
+        int o[32];
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const int4 t4 = offs[q4];
+          o[4 * q4 + 0] = t4.x;
+          o[4 * q4 + 1] = t4.y;
+          o[4 * q4 + 2] = t4.z;
+          o[4 * q4 + 3] = t4.w;
+        }
+        float v[32];
+#pragma unroll
+        for (int kk = 0; kk < 32; ++kk) v[kk] = (valid && o[kk] >= 0) ? halo[o[kk] + poff] : 0.f;
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int kk = 0; kk < 32; ++kk) {
+          s2 = fmaf(v[kk], v[kk], s2);
+          hi[kk] = tf32_hi_bits(v[kk]);
+          lo[kk] = __float_as_uint(v[kk] - __uint_as_float(hi[kk]));
+        }
+        const uint32_t acol = tmem + lane_off + kColA + st * 64;
         tmem_st16(acol, *reinterpret_cast<const uint32_t(*)[16]>(&hi[0]));
         tmem_st16(acol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&hi[16]));
         tmem_st16(acol + 32, *reinterpret_cast<const uint32_t(*)[16]>(&lo[0]));
         tmem_st16(acol + 48, *reinterpret_cast<const uint32_t(*)[16]>(&lo[16]));
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&S.a_full[sa]);
+        mbar_arrive(&S.a_full[st]);
       }
       if (!ok) break;
-      // hand S2 of this tile to the epilogue
       const uint32_t tb = (uint32_t)(li & 1), tph = (uint32_t)((li >> 1) & 1);
       if (!warp_wait(&S.s2_empty[tb], tph ^ 1, S.abort_flag)) {
         ok = false;
@@ -315,7 +326,6 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
       S.s2buf[tb * kTileM + r] = s2;
       mbar_arrive(&S.s2_full[tb]);
     }
-    cp_async_wait<0>();
   } else if (warp < 8) {
     // ---------------------------------------------------------- epilogue
     const int q = warp % 4;
@@ -338,7 +348,6 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
         }
         tc_fence_after();
         const uint32_t dcol = tmem + lane_off + slot * 128;
-        // 32 columns of H and of P per round, one wait per round
 #pragma unroll
         for (int jc = 0; jc < NB; jc += 32) {
           uint32_t hv[32], pv[32];
@@ -365,13 +374,10 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
       }
       const float s2 = S.s2buf[tb * kTileM + r];
       mbar_arrive(&S.s2_empty[tb]);
-      const int64_t g = t * kTileM + r;
-      const bool valid = g < p.NPQ;
-      int64_t obase = 0;
-      if (valid) {
-        const int64_t nn = g / p.PQ;
-        obase = nn * (int64_t)p.m * p.PQ + (g - nn * p.PQ);
-      }
+      const int64_t nimg = t / c.tpi;
+      const int pix = (int)(t - nimg * c.tpi) * kTileM + r;
+      const bool valid = pix < p.PQ;
+      const int64_t obase = nimg * (int64_t)p.m * p.PQ + pix;
 #pragma unroll
       for (int jj = 0; jj < NB; ++jj) {
         const int j = cb * NB + jj;
@@ -387,13 +393,13 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   } else if (warp == 8) {
     // ------------------------------------------------------------- MMA
     const uint32_t idesc = idesc_tf32(kTileM, 2 * NB);
-    const uint32_t sB_addr = smem_u32(S.sB);
-    uint32_t ita = 0, grp = 0;
+    const uint32_t stage_addr = smem_u32(S.stage);
+    uint32_t it = 0, grp = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
       uint32_t dcol = 0, slot = 0;
-      for (int kq = 0; kq < c.nKA; ++kq, ++ita) {
+      for (int kq = 0; kq < c.nK; ++kq, ++it) {
         const bool gstart = (kq % kGroupStages) == 0;
-        const bool gend = (kq % kGroupStages) == kGroupStages - 1 || kq == c.nKA - 1;
+        const bool gend = (kq % kGroupStages) == kGroupStages - 1 || kq == c.nK - 1;
         if (gstart) {
           slot = grp % kSlots;
           if (!warp_wait(&S.gr_empty[slot], ((grp / kSlots) & 1) ^ 1, S.abort_flag)) {
@@ -402,27 +408,24 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           }
           dcol = tmem + slot * 128;
         }
-        const uint32_t sa = ita % kAStages, pa = (ita / kAStages) & 1;
-        const uint32_t sb = ita % kBStages, pb = (ita / kBStages) & 1;
-        if (!warp_wait(&S.a_full[sa], pa, S.abort_flag) || !warp_wait(&S.b_full[sb], pb, S.abort_flag)) {
+        const uint32_t st = it % nst, ph = (it / nst) & 1;
+        if (!warp_wait(&S.a_full[st], ph, S.abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t ahi = tmem + kColA + sa * 64, alo = ahi + 32;
-          const uint32_t bhi = sB_addr + sb * bstage;                  // [H;P] rows, hi
-          const uint32_t blo = bhi + c.N * 128;                        // lo
+          const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
 #pragma unroll
-          for (int ks = 0; ks < kKA / 8; ++ks) {
-            const uint32_t ko = ks * 32;
+          for (int ks = 0; ks < kKS / 8; ++ks) {
+            const uint32_t bhi = stage_addr + st * c.sstage + ks * 32;  // [H;P] rows, hi
+            const uint32_t blo = bhi + c.N * 128;                       // lo
             const uint32_t acc = (gstart && ks == 0) ? 0u : 1u;
-            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(bhi + ko), idesc, acc);
-            mma_tf32_ts(dcol, alo + ks * 8, sdesc_kmajor_sw128(bhi + ko), idesc, 1u);
-            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(blo + ko), idesc, 1u);
+            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(bhi), idesc, acc);
+            mma_tf32_ts(dcol, alo + ks * 8, sdesc_kmajor_sw128(bhi), idesc, 1u);
+            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(blo), idesc, 1u);
           }
-          tc_commit(&S.a_empty[sa]);
-          tc_commit(&S.b_empty[sb]);
+          tc_commit(&S.s_empty[st]);
           if (gend) tc_commit(&S.gr_full[slot]);
         }
         __syncwarp();
@@ -434,28 +437,65 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
     __syncwarp();
     mbar_wait(S.final_bar, 0, kWaitNs, nullptr);
   } else {
-    // ---------------------------------------------------------- B loader
-    uint32_t itb = 0;
+    // ------------------------------------------------------------- loader
+    uint32_t it = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
-      const int cb = (int)(item % c.ncb);
-      for (int kc = 0; kc < c.nKB; ++kc, ++itb) {
-        const uint32_t sb = itb % kBStages, pb = (itb / kBStages) & 1;
-        if (!warp_wait(&S.b_empty[sb], pb ^ 1, S.abort_flag)) {
+      const int64_t t = item / c.ncb;
+      const int cb = (int)(item - t * c.ncb);
+      const TileGeo tg = tile_geo(p, c, t);
+      const float *ximg = x + tg.n * p.CHW + (int64_t)tg.ir0 * p.W;
+      const int64_t run = (int64_t)tg.rows * p.W;
+      for (int kq = 0; kq < c.nK; ++kq, ++it) {
+        const uint32_t st = it % nst, ph = (it / nst) & 1;
+        if (!warp_wait(&S.s_empty[st], ph ^ 1, S.abort_flag)) {
           ok = false;
           break;
         }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&S.b_full[sb], bstage);
-          bulk_g2s(S.sB + sb * bstage, wsB + ((int64_t)cb * c.nKB + kc) * 2 * c.N * 32, bstage, &S.b_full[sb]);
+        // Channel planes of the stage (one lane each): 16-byte-rounded spans,
+        // their leads and the total byte count.
+        const int clo = S.koff[kq * kKS].x;
+        int chi = clo;
+#pragma unroll 1
+        for (int kk = kKS - 1; kk >= 0; --kk) {
+          const int ch = S.koff[kq * kKS + kk].x;
+          if (ch >= 0) {
+            chi = ch;
+            break;
+          }
         }
+        const int nch = chi - clo + 1;
+        uint32_t bytes = 0;
+        tc::BulkSpan sp{};
+        if (lane < nch) {
+          sp = tc::bulk_span(ximg + (int64_t)(clo + lane) * p.HW, run);
+          S.lead[st * 32 + lane] = sp.lead;
+          bytes = sp.bytes;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
+        __syncwarp();
+        // Offset of every K of the stage inside the halo: plane, lead, tap.
+        {
+          const int2 ko = S.koff[kq * kKS + lane];
+          S.offs[st * kKS + lane] =
+              ko.x >= 0 ? (ko.x - clo) * c.PS + S.lead[st * 32 + (ko.x - clo)] + ko.y : -1;
+        }
+        __syncwarp();
+        uint8_t *sbase = S.stage + (size_t)st * c.sstage;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&S.full[st], c.bstage + bytes);
+          bulk_g2s(sbase, wsB + ((int64_t)cb * c.nK + kq) * 2 * c.N * 32, c.bstage, &S.full[st]);
+        }
+        __syncwarp();
+        if (lane < nch) bulk_g2s(sbase + c.bstage + (size_t)lane * c.PS * 4, sp.src, sp.bytes, &S.full[st]);
         __syncwarp();
       }
     }
     // Drain: the copies issued last have landed before the CTA exits.
-    const uint32_t last = std::min<uint32_t>(itb, kBStages);
+    const uint32_t last = it < (uint32_t)nst ? it : (uint32_t)nst;
     for (uint32_t i = 0; i < last; ++i) {
-      const uint32_t idx = itb - 1 - i;
-      mbar_wait(&S.b_full[idx % kBStages], (idx / kBStages) & 1, kWaitNs, nullptr);
+      const uint32_t idx = it - 1 - i;
+      mbar_wait(&S.full[idx % nst], (idx / nst) & 1, kWaitNs, nullptr);
     }
   }
 
@@ -500,7 +540,7 @@ int launch_forward(const Problem &p, const FwdCfg &c, const float *x, const floa
     }
   }
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
-  tc_forward_kernel<NB><<<grid, kFwdThreads, fwd_smem_bytes(c), stream>>>(x, pars, wsB, cj, factor, p, c, out, hsum,
+  tc_forward_kernel<NB><<<grid, kFwdThreads, fwd_smem_bytes(p, c), stream>>>(x, pars, wsB, cj, factor, p, c, out, hsum,
                                                                           status);
   PC2D_LAUNCH_CHECK("tc_forward_kernel");
   return PC2D_OK;
@@ -521,17 +561,19 @@ int device_sm_count() {
 }
 
 bool tc_forward_supported(const Problem &p) {
-  return p.m >= 1 && p.d <= kMaxD && p.CHW < ((int64_t)1 << 31) && p.NPQ > 0;
+  if (p.m < 1 || p.d > kMaxD || p.CHW >= ((int64_t)1 << 31) || p.NPQ <= 0 || p.PQ >= ((int64_t)1 << 30)) return false;
+  const FwdCfg c = fwd_cfg_fit(p);
+  return c.nchs <= 32 && fwd_smem_bytes(p, c) <= (size_t)kSmemLimit;
 }
 
 size_t tc_forward_workspace(const Problem &p) {
-  const FwdCfg c = fwd_cfg(p);
+  const FwdCfg c = fwd_cfg_fit(p);
   return align_up(fwd_bsplit_bytes(c), 256) + align_up((size_t)c.ncb * c.NB * sizeof(float), 256);
 }
 
 int tc_forward(const Problem &p, const float *x, const float *pars, double factor, float *out, float *hsum, void *ws,
                cudaStream_t stream) {
-  const FwdCfg c = fwd_cfg(p);
+  const FwdCfg c = fwd_cfg_fit(p);
   int *status = device_status_ptr();
   if (!status) {
     set_last_error("could not resolve the device status word");
@@ -539,7 +581,7 @@ int tc_forward(const Problem &p, const float *x, const float *pars, double facto
   }
   float *wsB = reinterpret_cast<float *>(ws);
   float *cj = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + align_up(fwd_bsplit_bytes(c), 256));
-  tc_fwd_prep_weights<<<dim3(c.nKB, c.ncb), 256, 0, stream>>>(pars, p, c, wsB);
+  tc_fwd_prep_weights<<<dim3(c.nK, c.ncb), 256, 0, stream>>>(pars, p, c, wsB);
   PC2D_LAUNCH_CHECK("tc_fwd_prep_weights");
   tc_fwd_prep_consts<<<ceil_div(c.ncb * c.NB, 8), 256, 0, stream>>>(pars, p, c, cj);
   PC2D_LAUNCH_CHECK("tc_fwd_prep_consts");
