@@ -468,9 +468,10 @@ size_t simt_backward_workspace(const Problem &p, bool) {
 template <typename T>
 int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, const T *hsum,
                   double factor, bool skip_input_grad, T *dx, T *dpars, void *ws, size_t ws_bytes,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, bool leave_dx) {
   const size_t npars = (size_t)p.m * 2 * (p.d + 1);
-  if (skip_input_grad || p.NPQ == 0) {
+  if (leave_dx) {
+  } else if (skip_input_grad || p.NPQ == 0) {
     if (p.NHW > 0) PC2D_CUDA_CHECK(cudaMemsetAsync(dx, 0, sizeof(T) * (size_t)p.NHW * p.C, stream));
   } else {
     const dim3 grid(ceil_div(p.NHW, DM), ceil_div(p.C, DC));
@@ -506,8 +507,8 @@ template int simt_forward<double>(const Problem &, const double *, const double 
 template size_t simt_backward_workspace<float>(const Problem &, bool);
 template size_t simt_backward_workspace<double>(const Problem &, bool);
 template int simt_backward<float>(const Problem &, const float *, const float *, const float *, const float *, double, bool,
-                                  float *, float *, void *, size_t, cudaStream_t);
+                                  float *, float *, void *, size_t, cudaStream_t, bool);
 template int simt_backward<double>(const Problem &, const double *, const double *, const double *, const double *, double,
-                                   bool, double *, double *, void *, size_t, cudaStream_t);
+                                   bool, double *, double *, void *, size_t, cudaStream_t, bool);
 
 }  // namespace pc2d

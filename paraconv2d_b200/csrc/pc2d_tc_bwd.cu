@@ -1,18 +1,505 @@
-// tcgen05 backward kernels of the ParaConv2d paraboloid convolution.
-// (The CUDA-core kernels in pc2d_simt.cu serve every backward problem until
-// the tensor-core wgrad/dgrad kernels land here.)
+// tcgen05 backward kernels of the ParaConv2d paraboloid convolution (fp32 via
+// 3xTF32 split precision).
+//
+// Input gradient (reference paraconv2d.cc:153-183):
+//   dx[c,y,x] = 2 * sum_{tap, o: window(o,tap) = (y,x)} sum_j
+//                 g[j,o] * (hsum[j,o] * h[j,c,tap] - x[c,y,x] + p[j,c,tap])
+//             = 2 * (sum_{tap,j} (g*hsum)[j,o] h[j,c,tap] + g[j,o] p[j,c,tap]
+//                    - x[c,y,x] * SG[y,x]),   SG = sum_{tap,j} g[j,o(tap)]
+// is an implicit GEMM with M = 128 input pixels of one image per tile,
+// N = input channels of a block (NC <= 64) and K = (j-block of 16 output
+// channels, tap, j, {g*hsum, g}) swept 32 at a time.  The windows are flipped
+// exactly as in the forward pass: tap (ix2, iy2) of output pixel (oy, ox)
+// reads input (oy*s0 + (k0-1-ix2)*dl0, ox*s1 + (k1-1-iy2)*dl1).
+//
+// Data movement:
+//   - the loader warp stages, per j-block, the rows of g and hsum the tile's
+//     windows reach (one 1-D bulk copy per output-channel plane, shared by
+//     the T taps of the j-block), and per 32-K stage the pre-split weights
+//     [W hi; W lo] (written once per call by a prep kernel);
+//   - producer warps (one TMEM lane = one input pixel) locate, per tap, the
+//     output pixel whose window covers them, form g*hsum and g for the 16
+//     channels of the stage, accumulate SG, split into tf32 hi + lo and
+//     tcgen05.st them into TMEM (A operand);
+//   - the MMA thread issues per 8-wide K step two MMAs:
+//       [main | corr] = Ahi * [W hi; W lo]   (N = 2 NC)
+//       corr         += Alo * W hi            (N = NC)
+//     so main + corr = Ahi*Bhi + Ahi*Blo + Alo*Bhi (3xTF32).
+//   - every 64 K start a fresh partial sum in one of two TMEM slots, which
+//     the epilogue warps drain into fp32 registers; the epilogue finally
+//     writes dx = 2 * (acc - x * SG).
+// Warp roles, barriers and the bounded-wait failure path are those of the
+// forward kernel (pc2d_tc_fwd.cu).
+#include <algorithm>
+#include <mutex>
+
 #include "pc2d_tc.cuh"
+#include "pc2d_tc_common.cuh"
 
 namespace pc2d {
 
-bool tc_backward_supported(const Problem &) { return false; }
+namespace {
+using namespace sm100;
+using tc::kWaitNs;
+using tc::warp_wait;
 
-size_t tc_backward_workspace(const Problem &, bool) { return 0; }
+constexpr int kTileM = 128;
+constexpr int kKS = 32;
+constexpr int kJB = 16;          // output channels per j-block (32 K per tap)
+constexpr int kStages = 4;
+constexpr int kSlots = 2;
+constexpr int kGroupStages = 2;
+constexpr int kMaxNC = 64;
+constexpr int kThreads = 320;
+constexpr int kMinSmem = 120 * 1024;
+constexpr int kSmemLimit = 227 * 1024;
+constexpr uint32_t kColA = 256;
 
-int tc_backward(const Problem &, const float *, const float *, const float *, const float *, double, bool, float *,
-                float *, void *, size_t, cudaStream_t) {
-  set_last_error("tensor-core backward not available");
-  return PC2D_ERR_UNSUPPORTED;
+struct DgCfg {
+  int ncb;          // input-channel blocks
+  int NC;           // channels per block (multiple of 16, <= 64)
+  int nJB;          // j-blocks
+  int nK;           // stages per tile = nJB * T
+  int nGroups;      // partial sums per tile
+  int tpi;          // tiles per image
+  int64_t tiles, items;
+  int PSo;          // g/hsum plane stride (floats, multiple of 4)
+  uint32_t bstage;  // B bytes per stage (hi + lo)
+  uint32_t jslot;   // bytes of a j-block slot (32 planes), multiple of 1024
+};
+
+DgCfg dg_cfg(const Problem &p) {
+  DgCfg c;
+  c.ncb = std::max(1, ceil_div(p.C, kMaxNC));
+  const int nc = ceil_div(p.C, c.ncb);
+  c.NC = (nc + 15) / 16 * 16;
+  c.nJB = ceil_div(p.m, kJB);
+  c.nK = c.nJB * p.T;
+  c.nGroups = ceil_div(c.nK, kGroupStages);
+  c.tpi = ceil_div(p.HW, kTileM);
+  c.tiles = (int64_t)p.n * c.tpi;
+  c.items = c.tiles * c.ncb;
+  const int irows = std::min<int64_t>(p.H, (p.W + kTileM - 2) / p.W + 1);
+  const int orows = std::min<int>(p.P, (irows - 1 + (p.k0 - 1) * p.dl0) / p.s0 + 2);
+  c.PSo = (int)(((int64_t)orows * p.Q + 8 + 3) / 4 * 4);
+  c.bstage = (uint32_t)(2 * c.NC * 128);
+  c.jslot = (uint32_t)align_up((size_t)2 * kJB * c.PSo * 4, 1024);
+  return c;
+}
+
+inline size_t dg_bsplit_bytes(const DgCfg &c) { return (size_t)c.ncb * c.nK * c.bstage; }
+inline size_t dg_smem_bytes(const DgCfg &c) {
+  size_t s = 1024 + (size_t)kStages * c.bstage + 2 * (size_t)c.jslot + 2 * 2 * kJB * 4 + 2 * kTileM * 4 + 24 * 8 + 64;
+  return std::max<size_t>(s, kMinSmem);
+}
+
+// Weights of input-channel block cb for stage kq = (jb, tap), split into
+// tf32 hi/lo, 128-byte-swizzled K-major: rows = channels (hi block then lo
+// block), K element kk = (j_local = kk/2, w = kk%2) holds h[j][c][tap]
+// (w = 0, multiplies g*hsum) or p[j][c][tap] (w = 1, multiplies g).
+__global__ void tc_dg_prep_weights(const float *__restrict__ pars, Problem p, DgCfg c, float *__restrict__ wsB) {
+  const int kq = blockIdx.x, cb = blockIdx.y;
+  const int jb = kq / p.T, tap = kq - (kq / p.T) * p.T;
+  float *blk = wsB + ((int64_t)cb * c.nK + kq) * 2 * c.NC * 32;
+  const float *h = pars + p.m;
+  const float *pp = h + (int64_t)p.m * p.d;
+  for (int e = threadIdx.x; e < c.NC * 32; e += blockDim.x) {
+    const int r = e / 32, kk = e % 32;
+    const int ch = cb * c.NC + r;
+    const int j = jb * kJB + kk / 2;
+    float v = 0.f;
+    if (ch < p.C && j < p.m) v = ((kk & 1) ? pp : h)[(int64_t)j * p.d + (int64_t)ch * p.T + tap];
+    const float hi = __uint_as_float(tf32_hi_bits(v));
+    const int pos = r * 32 + (((kk >> 2) ^ (r & 7)) << 2) + (kk & 3);
+    blk[pos] = hi;
+    blk[c.NC * 32 + pos] = v - hi;
+  }
+}
+
+struct DgGeo {
+  int64_t n;
+  int q0;      // first input pixel of the tile (within the image)
+  int oylo;    // first output row staged
+  int orows;   // output rows staged (may be 0)
+};
+
+__device__ __forceinline__ DgGeo dg_geo(const Problem &p, const DgCfg &c, int64_t t) {
+  DgGeo g;
+  g.n = t / c.tpi;
+  g.q0 = (int)(t - g.n * c.tpi) * kTileM;
+  const int qlast = min(g.q0 + kTileM - 1, (int)p.HW - 1);
+  const int iya = g.q0 / p.W, iyb = qlast / p.W;
+  const int lo = iya - (p.k0 - 1) * p.dl0;
+  int oylo = lo <= 0 ? 0 : (lo + p.s0 - 1) / p.s0;
+  int oyhi = min(p.P - 1, iyb / p.s0);
+  g.oylo = oylo;
+  g.orows = oyhi >= oylo ? oyhi - oylo + 1 : 0;
+  return g;
+}
+
+template <int NC>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, const float *__restrict__ hsum,
+                const float *__restrict__ wsB, Problem p, DgCfg c, float *__restrict__ dx, int *status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint8_t *sB = base;                                             // kStages x bstage
+  uint8_t *sJ = base + (size_t)kStages * c.bstage;                // 2 x jslot
+  int *jtab = reinterpret_cast<int *>(sJ + 2 * (size_t)c.jslot);  // [2][32] plane offsets (-1 = zero)
+  float *sgbuf = reinterpret_cast<float *>(jtab + 2 * 2 * kJB);   // [2][128]
+  uint64_t *bars = reinterpret_cast<uint64_t *>((reinterpret_cast<uintptr_t>(sgbuf + 2 * kTileM) + 7) & ~(uintptr_t)7);
+  uint64_t *full = bars, *a_full = bars + 4, *s_empty = bars + 8;
+  uint64_t *jfull = bars + 12, *jempty = bars + 14, *gr_full = bars + 16, *gr_empty = bars + 18;
+  uint64_t *sg_full = bars + 20, *sg_empty = bars + 22, *final_bar = bars + 24;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 25);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&a_full[i], 128);
+      mbar_init(&s_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&jfull[i], 1);
+      mbar_init(&jempty[i], 128);
+      mbar_init(&gr_full[i], 1);
+      mbar_init(&gr_empty[i], 128);
+      mbar_init(&sg_full[i], 128);
+      mbar_init(&sg_empty[i], 128);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  bool ok = true;
+
+  if (warp < 4) {
+    // ---------------------------------------------------------- producers
+    const int r = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    uint32_t it = 0, jit = 0;
+    int64_t li = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x, ++li) {
+      const DgGeo tg = dg_geo(p, c, item / c.ncb);
+      const int q = tg.q0 + r;
+      const bool pvalid = q < p.HW;
+      const int iy = q / p.W, ix = q - (q / p.W) * p.W;
+      float sg = 0.f;
+      for (int jb = 0; jb < c.nJB && ok; ++jb, ++jit) {
+        const uint32_t js = jit & 1, jph = (jit >> 1) & 1;
+        if (!warp_wait(&jfull[js], jph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const float *planes = reinterpret_cast<const float *>(sJ + (size_t)js * c.jslot);
+        int to[2 * kJB];
+#pragma unroll
+        for (int q4 = 0; q4 < 2 * kJB / 4; ++q4) {
+          const int4 t4 = reinterpret_cast<const int4 *>(jtab + js * 2 * kJB)[q4];
+          to[4 * q4 + 0] = t4.x;
+          to[4 * q4 + 1] = t4.y;
+          to[4 * q4 + 2] = t4.z;
+          to[4 * q4 + 3] = t4.w;
+        }
+        for (int tap = 0; tap < p.T; ++tap, ++it) {
+          const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+          if (!warp_wait(&full[st], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // output pixel whose window puts this tap on (iy, ix)
+          const int yy = iy - tap_row(p, tap), xx = ix - tap_col(p, tap);
+          bool valid = pvalid && yy >= 0 && xx >= 0;
+          int ooff = 0;
+          if (valid) {
+            const int oy = yy / p.s0, ox = xx / p.s1;
+            valid = (oy * p.s0 == yy) && (ox * p.s1 == xx) && oy < p.P && ox < p.Q;
+            ooff = (oy - tg.oylo) * p.Q + ox;
+          }
+          uint32_t hi[kKS], lo[kKS];
+#pragma unroll
+          for (int jl = 0; jl < kJB; ++jl) {
+            const int og = to[2 * jl], oh = to[2 * jl + 1];
+            const float gv = (valid && og >= 0) ? planes[og + ooff] : 0.f;
+            const float hv = (valid && oh >= 0) ? planes[oh + ooff] : 0.f;
+            sg += gv;
+            const float a0 = gv * hv, a1 = gv;
+            hi[2 * jl] = tf32_hi_bits(a0);
+            lo[2 * jl] = __float_as_uint(a0 - __uint_as_float(hi[2 * jl]));
+            hi[2 * jl + 1] = tf32_hi_bits(a1);
+            lo[2 * jl + 1] = __float_as_uint(a1 - __uint_as_float(hi[2 * jl + 1]));
+          }
+          const uint32_t acol = tmem + lane_off + kColA + st * 64;
+          tmem_st16(acol, *reinterpret_cast<const uint32_t(*)[16]>(&hi[0]));
+          tmem_st16(acol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&hi[16]));
+          tmem_st16(acol + 32, *reinterpret_cast<const uint32_t(*)[16]>(&lo[0]));
+          tmem_st16(acol + 48, *reinterpret_cast<const uint32_t(*)[16]>(&lo[16]));
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(&a_full[st]);
+        }
+        mbar_arrive(&jempty[js]);
+      }
+      if (!ok) break;
+      const uint32_t tb = (uint32_t)(li & 1), tph = (uint32_t)((li >> 1) & 1);
+      if (!warp_wait(&sg_empty[tb], tph ^ 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      sgbuf[tb * kTileM + r] = sg;
+      mbar_arrive(&sg_full[tb]);
+    }
+  } else if (warp < 8) {
+    // ---------------------------------------------------------- epilogue
+    const int qq = warp % 4;
+    const int r = qq * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(qq * 32) << 16;
+    uint32_t grp = 0;
+    int64_t li = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x, ++li) {
+      const int64_t t = item / c.ncb;
+      const int cb = (int)(item - t * c.ncb);
+      float acc[NC];
+#pragma unroll
+      for (int j = 0; j < NC; ++j) acc[j] = 0.f;
+      for (int gi = 0; gi < c.nGroups; ++gi, ++grp) {
+        const uint32_t slot = grp % kSlots, ph = (grp / kSlots) & 1;
+        if (!warp_wait(&gr_full[slot], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dcol = tmem + lane_off + slot * 128;
+#pragma unroll
+        for (int jc = 0; jc < NC; jc += 32) {
+          uint32_t mv[32], cv[32];
+          tmem_ld32_nowait(dcol + jc, mv);
+          tmem_ld32_nowait(dcol + NC + jc, cv);
+          tmem_ld_wait_tie(mv);
+          tmem_ld_wait_tie(cv);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj)
+            if (jc + jj < NC) acc[jc + jj] += __uint_as_float(mv[jj]) + __uint_as_float(cv[jj]);
+        }
+        tc_fence_before();
+        mbar_arrive(&gr_empty[slot]);
+      }
+      if (!ok) break;
+      const uint32_t tb = (uint32_t)(li & 1), tph = (uint32_t)((li >> 1) & 1);
+      if (!warp_wait(&sg_full[tb], tph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const float sg = sgbuf[tb * kTileM + r];
+      mbar_arrive(&sg_empty[tb]);
+      const int64_t nimg = t / c.tpi;
+      const int q = (int)(t - nimg * c.tpi) * kTileM + r;
+      if (q < p.HW) {
+        const int64_t xb = nimg * p.CHW + q;
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc) {
+          const int ch = cb * NC + cc;
+          if (ch < p.C) {
+            const int64_t xi = xb + (int64_t)ch * p.HW;
+            dx[xi] = 2.f * (acc[cc] - __ldg(x + xi) * sg);
+          }
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------- MMA
+    const uint32_t id_main = idesc_tf32(kTileM, 2 * NC);
+    const uint32_t id_corr = idesc_tf32(kTileM, NC);
+    const uint32_t sB_addr = smem_u32(sB);
+    uint32_t it = 0, grp = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
+      uint32_t dcol = 0, slot = 0;
+      for (int kq = 0; kq < c.nK; ++kq, ++it) {
+        const bool gstart = (kq % kGroupStages) == 0;
+        const bool gend = (kq % kGroupStages) == kGroupStages - 1 || kq == c.nK - 1;
+        if (gstart) {
+          slot = grp % kSlots;
+          if (!warp_wait(&gr_empty[slot], ((grp / kSlots) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          dcol = tmem + slot * 128;
+        }
+        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (!warp_wait(&a_full[st], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
+#pragma unroll
+          for (int ks = 0; ks < kKS / 8; ++ks) {
+            const uint32_t bhi = sB_addr + st * c.bstage + ks * 32;  // rows: W hi then W lo
+            const uint32_t acc = (gstart && ks == 0) ? 0u : 1u;
+            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(bhi), id_main, acc);
+            mma_tf32_ts(dcol + NC, alo + ks * 8, sdesc_kmajor_sw128(bhi), id_corr, 1u);
+          }
+          tc_commit(&s_empty[st]);
+          if (gend) tc_commit(&gr_full[slot]);
+        }
+        __syncwarp();
+        if (gend) ++grp;
+      }
+    }
+    if (lane == 0) tc_commit(final_bar);
+    __syncwarp();
+    mbar_wait(final_bar, 0, kWaitNs, nullptr);
+  } else {
+    // ------------------------------------------------------------- loader
+    uint32_t it = 0, jit = 0, jissued = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
+      const int64_t t = item / c.ncb;
+      const int cb = (int)(item - t * c.ncb);
+      const DgGeo tg = dg_geo(p, c, t);
+      const int64_t run = (int64_t)tg.orows * p.Q;
+      for (int jb = 0; jb < c.nJB && ok; ++jb, ++jit) {
+        const uint32_t js = jit & 1, jph = (jit >> 1) & 1;
+        if (!warp_wait(&jempty[js], jph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // lane l: plane l of the j-block = channel jb*16 + l/2, g (l even) or hsum (l odd)
+        const int j = jb * kJB + lane / 2;
+        const bool have = (j < p.m) && run > 0;
+        tc::BulkSpan sp{};
+        uint32_t bytes = 0;
+        if (have) {
+          const float *src = ((lane & 1) ? hsum : grad) + (tg.n * p.m + j) * p.PQ + (int64_t)tg.oylo * p.Q;
+          sp = tc::bulk_span(src, run);
+          bytes = sp.bytes;
+        }
+        jtab[js * 2 * kJB + lane] = have ? lane * c.PSo + sp.lead : -1;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&jfull[js], bytes);
+        __syncwarp();
+        if (have) bulk_g2s(sJ + (size_t)js * c.jslot + (size_t)lane * c.PSo * 4, sp.src, sp.bytes, &jfull[js]);
+        __syncwarp();
+        ++jissued;
+        for (int tap = 0; tap < p.T; ++tap, ++it) {
+          const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+          if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[st], c.bstage);
+            bulk_g2s(sB + (size_t)st * c.bstage, wsB + ((int64_t)cb * c.nK + jb * p.T + tap) * 2 * c.NC * 32,
+                     c.bstage, &full[st]);
+          }
+          __syncwarp();
+        }
+      }
+    }
+    // Drain: the copies issued last have landed before the CTA exits.
+    const uint32_t last = it < (uint32_t)kStages ? it : (uint32_t)kStages;
+    for (uint32_t i = 0; i < last; ++i) {
+      const uint32_t idx = it - 1 - i;
+      mbar_wait(&full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
+    }
+    const uint32_t jlast = jissued < 2u ? jissued : 2u;
+    for (uint32_t i = 0; i < jlast; ++i) {
+      const uint32_t idx = jissued - 1 - i;
+      mbar_wait(&jfull[idx & 1], (idx >> 1) & 1, kWaitNs, nullptr);
+    }
+  }
+
+  if (!ok) {
+    if (lane == 0) record_device_error(status, PC2D_ERR_TIMEOUT);
+    *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+std::mutex g_attr_mutex;
+bool g_attr_set[64][4] = {};
+
+template <int NC>
+int launch_dgrad(const Problem &p, const DgCfg &c, const float *grad, const float *x, const float *hsum,
+                 const float *wsB, float *dx, int *status, cudaStream_t stream) {
+  int dev = 0;
+  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (dev >= 0 && dev < 64 && !g_attr_set[dev][NC / 16 - 1]) {
+      PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_dgrad_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+      g_attr_set[dev][NC / 16 - 1] = true;
+    }
+  }
+  const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
+  tc_dgrad_kernel<NC><<<grid, kThreads, dg_smem_bytes(c), stream>>>(grad, x, hsum, wsB, p, c, dx, status);
+  PC2D_LAUNCH_CHECK("tc_dgrad_kernel");
+  return PC2D_OK;
+}
+
+bool dg_supported(const Problem &p) {
+  if (p.NPQ <= 0 || p.m < 1 || p.HW >= ((int64_t)1 << 30) || p.PQ >= ((int64_t)1 << 30)) return false;
+  const DgCfg c = dg_cfg(p);
+  return dg_smem_bytes(c) <= (size_t)kSmemLimit && c.PSo * 2 * kJB < (1 << 30);
+}
+
+}  // namespace
+
+bool tc_backward_supported(const Problem &p) { return dg_supported(p); }
+
+size_t tc_backward_workspace(const Problem &p, bool skip_input_grad) {
+  size_t ws = simt_backward_workspace<float>(p, skip_input_grad);
+  if (!skip_input_grad) ws = align_up(ws, 256) + align_up(dg_bsplit_bytes(dg_cfg(p)), 256);
+  return ws;
+}
+
+int tc_backward(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum,
+                double factor, bool skip_input_grad, float *dx, float *dpars, void *ws, size_t ws_bytes,
+                cudaStream_t stream) {
+  const size_t simt_ws = align_up(simt_backward_workspace<float>(p, skip_input_grad), 256);
+  if (!skip_input_grad && p.NPQ > 0) {
+    int *status = device_status_ptr();
+    if (!status) {
+      set_last_error("could not resolve the device status word");
+      return PC2D_ERR_CUDA;
+    }
+    const DgCfg c = dg_cfg(p);
+    float *wsB = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + simt_ws);
+    tc_dg_prep_weights<<<dim3(c.nK, c.ncb), 256, 0, stream>>>(pars, p, c, wsB);
+    PC2D_LAUNCH_CHECK("tc_dg_prep_weights");
+    int st = PC2D_OK;
+    switch (c.NC) {
+      case 16: st = launch_dgrad<16>(p, c, grad, x, hsum, wsB, dx, status, stream); break;
+      case 32: st = launch_dgrad<32>(p, c, grad, x, hsum, wsB, dx, status, stream); break;
+      case 48: st = launch_dgrad<48>(p, c, grad, x, hsum, wsB, dx, status, stream); break;
+      case 64: st = launch_dgrad<64>(p, c, grad, x, hsum, wsB, dx, status, stream); break;
+      default: set_last_error("internal: unsupported channel block %d", c.NC); return PC2D_ERR_UNSUPPORTED;
+    }
+    if (st != PC2D_OK) return st;
+  }
+  // Parameter gradients: CUDA-core wgrad; the input gradient was written above
+  // (or is zero-filled there when skip_input_grad).
+  const bool dx_done = !skip_input_grad && p.NPQ > 0;
+  return simt_backward<float>(p, grad, x, pars, hsum, factor, skip_input_grad, dx, dpars, ws, simt_ws, stream,
+                              /*leave_dx=*/dx_done);
 }
 
 }  // namespace pc2d
