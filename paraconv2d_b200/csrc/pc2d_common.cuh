@@ -65,11 +65,12 @@ int simt_forward(const Problem &p, const T *x, const T *pars, double factor, T *
                  cudaStream_t stream);
 template <typename T>
 size_t simt_backward_workspace(const Problem &p, bool skip_input_grad);
-// With leave_dx the input gradient is neither computed nor written.
+// With leave_dx the input gradient is neither computed nor written; with
+// skip_wgrad only the input gradient is computed.
 template <typename T>
 int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, const T *hsum,
                   double factor, bool skip_input_grad, T *dx, T *dpars, void *ws, size_t ws_bytes,
-                  cudaStream_t stream, bool leave_dx = false);
+                  cudaStream_t stream, bool leave_dx = false, bool skip_wgrad = false);
 
 }  // namespace pc2d
 

@@ -468,7 +468,7 @@ size_t simt_backward_workspace(const Problem &p, bool) {
 template <typename T>
 int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, const T *hsum,
                   double factor, bool skip_input_grad, T *dx, T *dpars, void *ws, size_t ws_bytes,
-                  cudaStream_t stream, bool leave_dx) {
+                  cudaStream_t stream, bool leave_dx, bool skip_wgrad) {
   const size_t npars = (size_t)p.m * 2 * (p.d + 1);
   if (leave_dx) {
   } else if (skip_input_grad || p.NPQ == 0) {
@@ -478,7 +478,7 @@ int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, co
     simt_dgrad_kernel<T><<<grid, kThreads, 0, stream>>>(grad, x, pars, hsum, p, dx);
     PC2D_LAUNCH_CHECK("simt_dgrad_kernel");
   }
-  if (npars == 0) return PC2D_OK;
+  if (npars == 0 || skip_wgrad) return PC2D_OK;
   if (p.NPQ == 0) {
     PC2D_CUDA_CHECK(cudaMemsetAsync(dpars, 0, sizeof(T) * npars, stream));
     return PC2D_OK;
@@ -507,8 +507,8 @@ template int simt_forward<double>(const Problem &, const double *, const double 
 template size_t simt_backward_workspace<float>(const Problem &, bool);
 template size_t simt_backward_workspace<double>(const Problem &, bool);
 template int simt_backward<float>(const Problem &, const float *, const float *, const float *, const float *, double, bool,
-                                  float *, float *, void *, size_t, cudaStream_t, bool);
+                                  float *, float *, void *, size_t, cudaStream_t, bool, bool);
 template int simt_backward<double>(const Problem &, const double *, const double *, const double *, const double *, double,
-                                   bool, double *, double *, void *, size_t, cudaStream_t, bool);
+                                   bool, double *, double *, void *, size_t, cudaStream_t, bool, bool);
 
 }  // namespace pc2d

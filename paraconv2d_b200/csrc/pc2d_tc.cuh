@@ -18,6 +18,12 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
                 double factor, bool skip_input_grad, float *dx, float *dpars, void *ws, size_t ws_bytes,
                 cudaStream_t stream);
 
+// Parameter-gradient GEMM and its reduction (pc2d_tc_wgrad.cu).
+bool tc_wgrad_supported(const Problem &p);
+size_t tc_wgrad_workspace(const Problem &p);
+int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, double factor,
+             float *dpars, void *ws, cudaStream_t stream);
+
 // A kernel that waits on an mbarrier nothing completes, bounded by timeout_us.
 int tc_selftest_bounded_wait(unsigned int timeout_us, int *status, cudaStream_t stream);
 

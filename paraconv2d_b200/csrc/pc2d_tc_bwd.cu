@@ -463,26 +463,38 @@ bool dg_supported(const Problem &p) {
 
 }  // namespace
 
-bool tc_backward_supported(const Problem &p) { return dg_supported(p); }
+bool tc_backward_supported(const Problem &p) { return dg_supported(p) || tc_wgrad_supported(p); }
+
+namespace {
+// Workspace layout: [parameter-gradient scratch | dgrad weights]
+size_t wgrad_scratch(const Problem &p, bool skip_input_grad) {
+  return align_up(tc_wgrad_supported(p) ? tc_wgrad_workspace(p) : simt_backward_workspace<float>(p, skip_input_grad),
+                  256);
+}
+}  // namespace
 
 size_t tc_backward_workspace(const Problem &p, bool skip_input_grad) {
-  size_t ws = simt_backward_workspace<float>(p, skip_input_grad);
-  if (!skip_input_grad) ws = align_up(ws, 256) + align_up(dg_bsplit_bytes(dg_cfg(p)), 256);
+  size_t ws = wgrad_scratch(p, skip_input_grad);
+  if (!skip_input_grad && dg_supported(p)) ws += align_up(dg_bsplit_bytes(dg_cfg(p)), 256);
   return ws;
 }
 
 int tc_backward(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum,
                 double factor, bool skip_input_grad, float *dx, float *dpars, void *ws, size_t ws_bytes,
                 cudaStream_t stream) {
-  const size_t simt_ws = align_up(simt_backward_workspace<float>(p, skip_input_grad), 256);
-  if (!skip_input_grad && p.NPQ > 0) {
+  const size_t wscr = wgrad_scratch(p, skip_input_grad);
+  bool dx_done = false;
+  if (skip_input_grad || p.NPQ == 0) {
+    if (p.NHW > 0) PC2D_CUDA_CHECK(cudaMemsetAsync(dx, 0, sizeof(float) * (size_t)p.NHW * p.C, stream));
+    dx_done = true;
+  } else if (dg_supported(p)) {
     int *status = device_status_ptr();
     if (!status) {
       set_last_error("could not resolve the device status word");
       return PC2D_ERR_CUDA;
     }
     const DgCfg c = dg_cfg(p);
-    float *wsB = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + simt_ws);
+    float *wsB = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + wscr);
     tc_dg_prep_weights<<<dim3(c.nK, c.ncb), 256, 0, stream>>>(pars, p, c, wsB);
     PC2D_LAUNCH_CHECK("tc_dg_prep_weights");
     int st = PC2D_OK;
@@ -494,11 +506,18 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
       default: set_last_error("internal: unsupported channel block %d", c.NC); return PC2D_ERR_UNSUPPORTED;
     }
     if (st != PC2D_OK) return st;
+    dx_done = true;
   }
-  // Parameter gradients: CUDA-core wgrad; the input gradient was written above
-  // (or is zero-filled there when skip_input_grad).
-  const bool dx_done = !skip_input_grad && p.NPQ > 0;
-  return simt_backward<float>(p, grad, x, pars, hsum, factor, skip_input_grad, dx, dpars, ws, simt_ws, stream,
+  if (p.NPQ > 0 && tc_wgrad_supported(p)) {
+    if (!dx_done) {
+      // input gradient on the CUDA cores, then the tensor-core parameter gradients
+      const int st = simt_backward<float>(p, grad, x, pars, hsum, factor, false, dx, dpars, nullptr, 0, stream,
+                                          /*leave_dx=*/false, /*skip_wgrad=*/true);
+      if (st != PC2D_OK) return st;
+    }
+    return tc_wgrad(p, grad, x, pars, hsum, factor, dpars, ws, stream);
+  }
+  return simt_backward<float>(p, grad, x, pars, hsum, factor, skip_input_grad, dx, dpars, ws, wscr, stream,
                               /*leave_dx=*/dx_done);
 }
 

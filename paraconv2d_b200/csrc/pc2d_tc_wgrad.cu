@@ -1,0 +1,455 @@
+// tcgen05 parameter-gradient kernel of the ParaConv2d paraboloid convolution
+// (fp32 via 3xTF32 split precision) and its fixed-order reduction.
+//
+// Parameter gradients (reference paraconv2d.cc:186-237):
+//   dh[j,k]  = 2f sum_o (g*hsum)[j,o] win_o[k]     dh0[j] = 2f sum_o (g*hsum)[j,o]
+//   dp[j,k]  = 2f (sum_o g[j,o] win_o[k] - p[j,k] sum_o g[j,o])
+//   dp0[j]   = 2f (-p0[j]) sum_o g[j,o]
+// The two contractions are one GEMM over the output pixels o:
+//   D[r, k] = sum_o A[r, o] * win_o[k],  A = [g*hsum (JM rows); g (JM rows)]
+// with M = 128 rows (a block of JM <= 64 output channels), N = a range of
+// NR <= 256 window elements k = (c, tap) and K = output pixels, swept in
+// 32-pixel chunks of one image; the pixels are split into segments across
+// CTAs.
+//
+// Per 32-pixel chunk:
+//   - four A-producer warps (one TMEM lane = one row r) load the 32 values
+//     of their row with vector loads, form g*hsum or g, accumulate the row
+//     sum, split into tf32 hi + lo and tcgen05.st them into TMEM;
+//   - eight B-producer warps (one lane = one pixel of the chunk) gather the
+//     flipped windows of the chunk's pixels (coalesced across the pixels of a
+//     warp), split them and store rows k of the 128-byte-swizzled K-major B
+//     operand in shared memory;
+//   - the MMA thread issues Ahi*Bhi + Alo*Bhi + Ahi*Blo (N = NR) per 8
+//     pixels.
+// At the end of a segment the epilogue warps drain the fp32 accumulator to a
+// per-segment slice of the workspace (a partial over at most 1024 pixels, so
+// the tensor core's per-instruction accumulation error stays small); a second
+// kernel sums the slices in a fixed order in fp64 and applies the epilogue
+// above.  No floating-point atomics: the result is deterministic.
+//
+// Warp roles (544 threads, one CTA per SM): warps 0-3 A producers, 4-11 B
+// producers, 12-15 epilogue, 16 MMA issuer and TMEM owner.  All waits are
+// bounded as in the forward kernel.
+#include <algorithm>
+#include <mutex>
+
+#include "pc2d_tc.cuh"
+#include "pc2d_tc_common.cuh"
+
+namespace pc2d {
+
+namespace {
+using namespace sm100;
+using tc::kWaitNs;
+using tc::warp_wait;
+
+constexpr int kChunk = 32;        // pixels per K chunk
+constexpr int kStages = 3;
+constexpr int kMaxSeg = 32;       // chunks per segment
+constexpr int kThreads = 544;
+constexpr int kBWarps = 8;
+constexpr int kMinSmem = 120 * 1024;
+constexpr int kSmemLimit = 227 * 1024;
+constexpr uint32_t kColA = 256;   // A stages at 256 + 64 * stage
+
+struct WgCfg {
+  int nmb, JM;      // output-channel blocks, channels per block
+  int nNR, NR;      // window-row ranges, rows per range (multiple of 16, <= 256)
+  int cpi;          // 32-pixel chunks per image
+  int64_t chunks;   // n * cpi
+  int SEG;          // chunks per segment
+  int64_t nseg;
+  int64_t items;    // nseg * nNR * nmb
+  uint32_t bstage;  // B bytes per stage (hi + lo)
+};
+
+WgCfg wg_cfg(const Problem &p, int sms) {
+  WgCfg c;
+  c.nmb = std::max(1, ceil_div(p.m, 64));
+  c.JM = ceil_div(p.m, c.nmb);
+  c.nNR = std::max(1, ceil_div(p.d, 256));
+  c.NR = (ceil_div(p.d, c.nNR) + 15) / 16 * 16;
+  c.cpi = ceil_div(p.PQ, kChunk);
+  c.chunks = (int64_t)p.n * c.cpi;
+  const int64_t per = (int64_t)c.nNR * c.nmb;
+  int64_t seg = c.chunks * per / std::max<int64_t>(1, 2 * sms);
+  c.SEG = (int)std::max<int64_t>(4, std::min<int64_t>(kMaxSeg, seg));
+  c.nseg = (c.chunks + c.SEG - 1) / c.SEG;
+  c.items = c.nseg * per;
+  c.bstage = (uint32_t)(2 * c.NR * 128);
+  return c;
+}
+
+inline size_t wg_smem_bytes(const WgCfg &c) {
+  size_t s = 1024 + (size_t)kStages * c.bstage + 16 * 8 + 64;
+  return std::max<size_t>(s, kMinSmem);
+}
+inline size_t wg_part_bytes(const WgCfg &c) { return align_up((size_t)c.items * 128 * c.NR * 4, 256); }
+inline size_t wg_sums_bytes(const WgCfg &c) { return align_up((size_t)c.items * 128 * 4, 256); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, const float *__restrict__ hsum,
+                Problem p, WgCfg c, float *__restrict__ part, float *__restrict__ sums, int *status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint8_t *sB = base;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + (size_t)kStages * c.bstage);
+  uint64_t *a_full = bars, *a_empty = bars + 3, *b_full = bars + 6, *b_empty = bars + 9;
+  uint64_t *d_full = bars + 12, *d_empty = bars + 13, *final_bar = bars + 14;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 15);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&a_full[i], 128);
+      mbar_init(&a_empty[i], 1);
+      mbar_init(&b_full[i], kBWarps);
+      mbar_init(&b_empty[i], 1);
+    }
+    mbar_init(d_full, 1);
+    mbar_init(d_empty, 128);
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 16) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int per = c.nNR * c.nmb;
+  bool ok = true;
+
+  if (warp < 4) {
+    // -------------------------------------------------------- A producers
+    const int r = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(grad) | reinterpret_cast<uintptr_t>(hsum)) & 15) == 0 &&
+                        (p.PQ % 4) == 0;
+    uint32_t it = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
+      const int64_t seg = item / per;
+      const int mb = (int)((item - seg * per) % c.nmb);
+      const int w = r < c.JM ? 0 : 1;
+      const int j = mb * c.JM + (r - w * c.JM);
+      const bool rvalid = r < 2 * c.JM && j < p.m;
+      float rowsum = 0.f;
+      const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
+      for (int64_t gc = g0; gc < g1; ++gc, ++it) {
+        const int64_t n = gc / c.cpi;
+        const int pq0 = (int)(gc - n * c.cpi) * kChunk;
+        const int npx = min(kChunk, (int)p.PQ - pq0);
+        float v[kChunk];
+        if (rvalid) {
+          const int64_t off = (n * p.m + j) * p.PQ + pq0;
+          if (vec_ok && npx == kChunk) {
+            const float4 *gp = reinterpret_cast<const float4 *>(grad + off);
+#pragma unroll
+            for (int q = 0; q < kChunk / 4; ++q) {
+              const float4 t4 = __ldg(gp + q);
+              v[4 * q] = t4.x;
+              v[4 * q + 1] = t4.y;
+              v[4 * q + 2] = t4.z;
+              v[4 * q + 3] = t4.w;
+            }
+            if (w == 0) {
+              const float4 *hp = reinterpret_cast<const float4 *>(hsum + off);
+#pragma unroll
+              for (int q = 0; q < kChunk / 4; ++q) {
+                const float4 t4 = __ldg(hp + q);
+                v[4 * q] *= t4.x;
+                v[4 * q + 1] *= t4.y;
+                v[4 * q + 2] *= t4.z;
+                v[4 * q + 3] *= t4.w;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < kChunk; ++q) {
+              float a = 0.f;
+              if (q < npx) {
+                a = __ldg(grad + off + q);
+                if (w == 0) a *= __ldg(hsum + off + q);
+              }
+              v[q] = a;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < kChunk; ++q) v[q] = 0.f;
+        }
+        uint32_t hi[kChunk], lo[kChunk];
+#pragma unroll
+        for (int q = 0; q < kChunk; ++q) {
+          rowsum += v[q];
+          hi[q] = tf32_hi_bits(v[q]);
+          lo[q] = __float_as_uint(v[q] - __uint_as_float(hi[q]));
+        }
+        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (!warp_wait(&a_empty[st], ph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acol = tmem + lane_off + kColA + st * 64;
+        tmem_st16(acol, *reinterpret_cast<const uint32_t(*)[16]>(&hi[0]));
+        tmem_st16(acol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&hi[16]));
+        tmem_st16(acol + 32, *reinterpret_cast<const uint32_t(*)[16]>(&lo[0]));
+        tmem_st16(acol + 48, *reinterpret_cast<const uint32_t(*)[16]>(&lo[16]));
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&a_full[st]);
+      }
+      sums[item * 128 + r] = rowsum;
+    }
+  } else if (warp < 4 + kBWarps) {
+    // -------------------------------------------------------- B producers
+    // Warp bw builds rows kl = bw + 8*i of each chunk's B tile; lane i holds
+    // the input offset of row bw + 8*i of the item's window range.
+    const int bw = warp - 4;
+    const int nrows = (c.NR - bw + kBWarps - 1) / kBWarps;  // <= 32
+    uint32_t it = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
+      const int64_t seg = item / per;
+      const int nr = (int)((item - seg * per) / c.nmb);
+      int myoff = -1;
+      {
+        const int kl = bw + kBWarps * lane;
+        const int64_t k = (int64_t)nr * c.NR + kl;
+        if (kl < c.NR && k < p.d) {
+          const int ch = (int)(k / p.T), tap = (int)(k - (int64_t)ch * p.T);
+          myoff = ch * (int)p.HW + tap_row(p, tap) * p.W + tap_col(p, tap);
+        }
+      }
+      const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
+      for (int64_t gc = g0; gc < g1; ++gc, ++it) {
+        const int64_t n = gc / c.cpi;
+        const int pq = (int)(gc - n * c.cpi) * kChunk + lane;
+        const bool pvalid = pq < p.PQ;
+        int64_t pbase = 0;
+        if (pvalid) {
+          const int oy = pq / p.Q, ox = pq - (pq / p.Q) * p.Q;
+          pbase = n * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
+        }
+        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (!warp_wait(&b_empty[st], ph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t *stg = sB + (size_t)st * c.bstage;
+        const uint32_t cpos = (uint32_t)(lane & 3) * 4;
+        for (int i0 = 0; i0 < nrows; i0 += 4) {
+          float v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int o = __shfl_sync(0xffffffffu, myoff, (i0 + u) & 31);
+            v[u] = (i0 + u < nrows && pvalid && o >= 0) ? __ldg(x + pbase + o) : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (i0 + u < nrows) {
+              const uint32_t kl = (uint32_t)(bw + kBWarps * (i0 + u));
+              const uint32_t hb = tf32_hi_bits(v[u]);
+              const uint32_t off = kl * 128 + ((((uint32_t)lane >> 2) ^ (kl & 7)) << 4) + cpos;
+              *reinterpret_cast<uint32_t *>(stg + off) = hb;
+              *reinterpret_cast<float *>(stg + (size_t)c.NR * 128 + off) = v[u] - __uint_as_float(hb);
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b_full[st]);
+      }
+    }
+  } else if (warp < 16) {
+    // ----------------------------------------------------------- epilogue
+    const int q = warp % 4;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    uint32_t di = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x, ++di) {
+      if (!warp_wait(d_full, di & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float *dst = part + ((size_t)item * 128 + r) * c.NR;
+      for (int cc = 0; cc < c.NR; cc += 32) {
+        uint32_t vv[32];
+        tmem_ld32_nowait(tmem + lane_off + cc, vv);
+        tmem_ld_wait_tie(vv);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          if (cc + 4 * q4 < c.NR)
+            reinterpret_cast<float4 *>(dst + cc)[q4] =
+                make_float4(__uint_as_float(vv[4 * q4]), __uint_as_float(vv[4 * q4 + 1]),
+                            __uint_as_float(vv[4 * q4 + 2]), __uint_as_float(vv[4 * q4 + 3]));
+      }
+      tc_fence_before();
+      mbar_arrive(d_empty);
+    }
+  } else {
+    // ---------------------------------------------------------------- MMA
+    const uint32_t idesc = idesc_tf32(128, c.NR);
+    const uint32_t sB_addr = smem_u32(sB);
+    uint32_t it = 0, di = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x, ++di) {
+      if (!warp_wait(d_empty, (di & 1) ^ 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const int64_t seg = item / per;
+      const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
+      for (int64_t gc = g0; gc < g1; ++gc, ++it) {
+        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (!warp_wait(&a_full[st], ph, abort_flag) || !warp_wait(&b_full[st], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
+#pragma unroll
+          for (int ks = 0; ks < kChunk / 8; ++ks) {
+            const uint32_t bhi = sB_addr + st * c.bstage + ks * 32;
+            const uint32_t blo = bhi + c.NR * 128;
+            const uint32_t acc = (gc == g0 && ks == 0) ? 0u : 1u;
+            mma_tf32_ts(tmem, ahi + ks * 8, sdesc_kmajor_sw128(bhi), idesc, acc);
+            mma_tf32_ts(tmem, alo + ks * 8, sdesc_kmajor_sw128(bhi), idesc, 1u);
+            mma_tf32_ts(tmem, ahi + ks * 8, sdesc_kmajor_sw128(blo), idesc, 1u);
+          }
+          tc_commit(&a_empty[st]);
+          tc_commit(&b_empty[st]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit(d_full);
+      __syncwarp();
+    }
+    if (lane == 0) tc_commit(final_bar);
+    __syncwarp();
+    mbar_wait(final_bar, 0, kWaitNs, nullptr);
+  }
+
+  if (!ok) {
+    if (lane == 0) record_device_error(status, PC2D_ERR_TIMEOUT);
+    *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 16) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Fixed-order fp64 reduction of the per-segment partials and the parameter
+// gradient epilogue:  dh = 2f dH, dp = 2f (dP - p SG), dh0 = 2f S1,
+// dp0 = -2f p0 SG.  Grid (ceil(d/256), m).
+__global__ void __launch_bounds__(256)
+tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums, const float *__restrict__ pars,
+                  Problem p, WgCfg c, double f2, float *__restrict__ dpars) {
+  __shared__ double s_sums[2];
+  const int j = blockIdx.y;
+  const int64_t k = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  const int mb = j / c.JM, jl = j - mb * c.JM;
+  const int r1 = jl, r2 = c.JM + jl;
+  const int per = c.nNR * c.nmb;
+  if (threadIdx.x < 32) {
+    double a = 0.0, b = 0.0;
+    for (int64_t s = threadIdx.x; s < c.nseg; s += 32) {
+      const int64_t item = s * per + mb;  // nr = 0 slice carries the row sums
+      a += (double)sums[item * 128 + r1];
+      b += (double)sums[item * 128 + r2];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      a += __shfl_down_sync(0xffffffffu, a, off);
+      b += __shfl_down_sync(0xffffffffu, b, off);
+    }
+    if (threadIdx.x == 0) {
+      s_sums[0] = a;
+      s_sums[1] = b;
+    }
+  }
+  __syncthreads();
+  const double s1 = s_sums[0], sg = s_sums[1];
+  const int m = p.m;
+  const int64_t d = p.d;
+  const float *pp = pars + m + (int64_t)m * d;
+  const float *p0 = pp + (int64_t)m * d;
+  float *dh0 = dpars, *dh = dpars + m, *dpp = dh + (int64_t)m * d, *dp0 = dpp + (int64_t)m * d;
+  if (k < d) {
+    const int nr = (int)(k / c.NR);
+    const int kl = (int)(k - (int64_t)nr * c.NR);
+    double ah = 0.0, ap = 0.0;
+    for (int64_t s = 0; s < c.nseg; ++s) {
+      const int64_t item = (s * c.nNR + nr) * c.nmb + mb;
+      ah += (double)part[(item * 128 + r1) * c.NR + kl];
+      ap += (double)part[(item * 128 + r2) * c.NR + kl];
+    }
+    const int64_t wi = (int64_t)j * d + k;
+    dh[wi] = (float)(f2 * ah);
+    dpp[wi] = (float)(f2 * (ap - (double)pp[wi] * sg));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    dh0[j] = (float)(f2 * s1);
+    dp0[j] = (float)(f2 * (-(double)p0[j]) * sg);
+  }
+}
+
+std::mutex g_attr_mutex;
+bool g_attr_set[64] = {};
+
+}  // namespace
+
+bool tc_wgrad_supported(const Problem &p) {
+  if (p.NPQ <= 0 || p.m < 1 || p.CHW >= ((int64_t)1 << 31) || p.PQ >= ((int64_t)1 << 30)) return false;
+  const WgCfg c = wg_cfg(p, 148);
+  return wg_smem_bytes(c) <= (size_t)kSmemLimit && c.NR <= 256 && 2 * c.JM <= 128;
+}
+
+size_t tc_wgrad_workspace(const Problem &p) {
+  const WgCfg c = wg_cfg(p, device_sm_count());
+  return wg_part_bytes(c) + wg_sums_bytes(c);
+}
+
+int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, double factor,
+             float *dpars, void *ws, cudaStream_t stream) {
+  const WgCfg c = wg_cfg(p, device_sm_count());
+  int *status = device_status_ptr();
+  if (!status) {
+    set_last_error("could not resolve the device status word");
+    return PC2D_ERR_CUDA;
+  }
+  float *part = reinterpret_cast<float *>(ws);
+  float *sums = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + wg_part_bytes(c));
+  int dev = 0;
+  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (dev >= 0 && dev < 64 && !g_attr_set[dev]) {
+      PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+      g_attr_set[dev] = true;
+    }
+  }
+  const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
+  tc_wgrad_kernel<<<grid, kThreads, wg_smem_bytes(c), stream>>>(grad, x, hsum, p, c, part, sums, status);
+  PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
+  const dim3 fgrid(ceil_div(p.d, 256), p.m);
+  tc_wgrad_finalize<<<fgrid, 256, 0, stream>>>(part, sums, pars, p, c, 2.0 * (double)(float)factor, dpars);
+  PC2D_LAUNCH_CHECK("tc_wgrad_finalize");
+  return PC2D_OK;
+}
+
+}  // namespace pc2d
