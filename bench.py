@@ -16,8 +16,9 @@ GPU).  Output: one JSON line on rank 0.
             autograd backward), with the step's input and upstream gradient
             copied from pinned host memory and the parameter gradient read
             back, all inside the timed region
-  roofline  the dominant pass (forward or backward) against the 3xTF32
-            tensor peak (a measured TF32 GEMM rate / 3)
+  roofline  the dominant kernel (largest summed CUDA-event time in the timed
+            region, timed per launch by the library's pc2d_timing_* hooks)
+            against the 3xTF32 tensor peak (a measured TF32 GEMM rate / 3)
   cpu_baseline  the reference CPU op on the host cores (bounded sample)
 
 --impl reference times the reference's own CPU implementation of the op
@@ -46,10 +47,18 @@ METRIC = "fwd & fwd+bwd images/s (N=128, 64→64ch, 32×32, k3) on B200; % of ro
 UNIT = "images/s"
 L2_FLUSH_BYTES = 512 << 20
 
-# DRAM traffic per launch of the dominant kernel, from the ncu capture
-# summarised in profiles/ (dram__bytes_read.sum + dram__bytes_write.sum).
-# None until a capture of the current kernel exists.
-NCU_TRAFFIC_BYTES = {}
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
+# each main kernel on the c2 layer, from the ncu --set full capture summarised
+# in profiles/tc_kernels_c2.md.  Writes that are still in L2 when a kernel ends
+# are not counted by that capture.
+NCU_TRAFFIC_BYTES = {
+    ("c2", "forward"): 38.544896e6 + 15.991296e6,
+    ("c2", "dgrad"): 105.642496e6 + 16.875008e6,
+    ("c2", "wgrad"): 105.066496e6 + 10.518272e6,
+}
+
+# Kernel families the library can time (pc2d_timing_read).
+KERNELS = ("forward", "dgrad", "wgrad", "simt_forward", "simt_dgrad", "simt_wgrad")
 
 
 def parse_args():
@@ -95,7 +104,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
         return self
@@ -323,7 +332,11 @@ def run_ours(args):
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    lib.pc2d_timing_reset()
+    lib.pc2d_timing_enable(1)
+    clk = ClockSampler(local)
+    clk.__enter__()
+    if True:
         for i in range(args.steps):
             flush.zero_()
             ev[i][0].record(stream)
@@ -334,6 +347,8 @@ def run_ours(args):
             allreduce()
             ev[i][3].record(stream)
         torch.cuda.synchronize()
+    lib.pc2d_timing_enable(0)
+    ktimes = _lib.kernel_times(KERNELS)
     barrier()
     t_fwd = [e[0].elapsed_time(e[1]) / 1e3 for e in ev]
     t_bwd = [e[1].elapsed_time(e[2]) / 1e3 for e in ev]
@@ -380,12 +395,14 @@ def run_ours(args):
         e_e.synchronize()
         e_tot += e_s.elapsed_time(e_e) / 1e3
     e_tot = max_over_ranks(e_tot)
+    clk.__exit__(None, None, None)
     barrier()
     e2e_value = images / e_tot
     h2d = x_host.numel() * 4 + g_host.numel() * 4
     d2h = dp_host.numel() * 4
 
-    # ---- roofline of the dominant pass
+    # ---- roofline of the dominant kernel (per-launch CUDA-event times of
+    # the timed region; each main kernel does 4*m*d*n*P*Q algorithmic flops)
     peaks = measured_peaks()
     tf32 = measure_tf32_tflops(dev)
     peak_3x = tf32 / 3.0
@@ -393,15 +410,18 @@ def run_ours(args):
     f_bwd = workloads.bwd_flops_per_image(wl) * n
     mean_fwd = tot_fwd / args.steps
     mean_bwd = tot_bwd / args.steps
-    dom = "forward" if mean_fwd >= mean_bwd else "backward"
-    dom_t, dom_f = (mean_fwd, f_fwd) if dom == "forward" else (mean_bwd, f_bwd)
-    achieved = dom_f / dom_t / 1e12
+    timed = {k: v for k, v in ktimes.items() if v[1] > 0}
+    dom = max(timed, key=lambda k: timed[k][0]) if timed else "forward"
+    dom_ms = timed[dom][0] / timed[dom][1] if timed else 1e3 * mean_fwd
+    kflops = workloads.fwd_flops_per_image(wl) * n  # forward, dgrad and wgrad kernels alike
+    achieved = kflops / (dom_ms / 1e3) / 1e12
     fwd_frac = f_fwd / mean_fwd / 1e12 / peak_3x
     bwd_frac = f_bwd / mean_bwd / 1e12 / peak_3x
     tr = NCU_TRAFFIC_BYTES.get((args.workload, dom))
     roofline = {
         "bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s", "frac": achieved / peak_3x,
-        "traffic": tr, "kernel": dom,
+        "traffic": tr, "kernel": dom, "kernel_ms": dom_ms,
+        "kernel_ms_all": {k: v[0] / v[1] for k, v in timed.items()},
         "peak_source": f"measured TF32 cuBLAS GEMM {tf32:.0f} TFLOP/s on this GPU / 3 (3xTF32 issues three MMAs per "
                        f"algorithmic multiply-add); bf16 dense {peaks.get('bf16_tflops')} TFLOP/s of measured "
                        f"(MEASURED_PEAKS.json)",
@@ -430,7 +450,7 @@ def run_ours(args):
                        "algo": {0: "auto", 1: "simt", 2: "tc"}[lib.pc2d_get_algo()]},
             "fwd_images_per_s": fwd_value, "fwd_ms": 1e3 * mean_fwd, "bwd_ms": 1e3 * mean_bwd,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * launches_per_step(lib, wl),
+            "gpu_launches": args.steps * launches_per_step(lib, ktimes, args.steps),
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -440,13 +460,14 @@ def run_ours(args):
     return 0
 
 
-def launches_per_step(lib, wl):
-    """Our kernel launches per device-resident step: forward (tcgen05: 2 prep
-    + 1 main; CUDA-core: 1) and backward (3 CUDA-core kernels)."""
-    from paraconv2d_b200 import _lib
-    algo = lib.pc2d_get_algo()
-    fwd = 3 if algo != _lib.PC2D_ALGO_SIMT else 1
-    return fwd + 3
+def launches_per_step(lib, ktimes, steps):
+    """Our kernel launches per device-resident step, from the timed main
+    kernels: tcgen05 forward = 2 prep kernels + the main kernel; tcgen05
+    dgrad = 1 prep + main; tcgen05 wgrad = main + fixed-order reduction;
+    CUDA-core forward = 1; CUDA-core dgrad = 1; CUDA-core wgrad = 2."""
+    per_main = {"forward": 3, "dgrad": 2, "wgrad": 2, "simt_forward": 1, "simt_dgrad": 1, "simt_wgrad": 2}
+    total = sum(per_main[k] * v[1] for k, v in ktimes.items())
+    return total // max(1, steps)
 
 
 def main():

@@ -117,11 +117,22 @@ const char *pc2d_last_error(void);
 int pc2d_device_status(void);
 int pc2d_clear_device_status(void);
 
+/* Kernel timing (profiling aid, off by default).  While enabled, every main
+ * kernel the library launches is bracketed by two CUDA events recorded on its
+ * stream; pc2d_timing_read synchronises those events and returns, for the
+ * kernel family `kernel` ("forward", "dgrad", "wgrad", "simt_forward",
+ * "simt_dgrad", "simt_wgrad"), the summed duration in milliseconds and the
+ * launch count since the last reset.  Returns PC2D_OK, or
+ * PC2D_ERR_INVALID_ARGUMENT for an unknown name. */
+int pc2d_timing_enable(int on);
+int pc2d_timing_reset(void);
+int pc2d_timing_read(const char *kernel, double *total_ms, int *launches);
+
 /* Test hook: a kernel that waits on an mbarrier that nothing completes, with
- * a wait limit of `max_polls`; it must return by itself and record
- * PC2D_ERR_TIMEOUT.  Used to check the bounded-wait path without faulting or
- * hanging the GPU. */
-int pc2d_selftest_bounded_wait(unsigned int max_polls, void *stream);
+ * a wait limit of `timeout_us` microseconds; it must return by itself and
+ * record PC2D_ERR_TIMEOUT.  Used to check the bounded-wait path without
+ * faulting or hanging the GPU. */
+int pc2d_selftest_bounded_wait(unsigned int timeout_us, void *stream);
 
 #ifdef __cplusplus
 }

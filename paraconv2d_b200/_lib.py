@@ -83,6 +83,9 @@ def cabi() -> ctypes.CDLL:
             "pc2d_device_status": ([], I),
             "pc2d_clear_device_status": ([], I),
             "pc2d_selftest_bounded_wait": ([ctypes.c_uint, P], I),
+            "pc2d_timing_enable": ([I], I),
+            "pc2d_timing_reset": ([], I),
+            "pc2d_timing_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(lib, name)
@@ -103,3 +106,17 @@ def set_algo(algo: int) -> int:
     if prev < 0:
         raise ValueError(f"invalid algo {algo}")
     return prev
+
+
+def kernel_times(names=("forward", "dgrad", "wgrad", "simt_forward", "simt_dgrad", "simt_wgrad")):
+    """{family: (total_ms, launches)} recorded since the last pc2d_timing_reset."""
+    lib = cabi()
+    out = {}
+    for n in names:
+        t = ctypes.c_double(0.0)
+        c = ctypes.c_int(0)
+        st = lib.pc2d_timing_read(n.encode(), ctypes.byref(t), ctypes.byref(c))
+        if st != PC2D_OK:
+            raise RuntimeError(status_message(st))
+        out[n] = (t.value, c.value)
+    return out

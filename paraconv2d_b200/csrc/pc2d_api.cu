@@ -5,7 +5,9 @@
 #include <stdio.h>
 
 #include <atomic>
+#include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "pc2d_common.cuh"
 #include "pc2d_tc.cuh"
@@ -16,6 +18,32 @@ __device__ int g_device_status = 0;
 
 namespace {
 thread_local char t_last_error[512] = "";
+
+// ------------------------------------------------------------ kernel timing
+const char *const kKernelNames[K_COUNT] = {"forward", "dgrad", "wgrad", "simt_forward", "simt_dgrad", "simt_wgrad"};
+struct TimingState {
+  std::mutex mu;
+  bool on = false;
+  std::vector<cudaEvent_t> pool;  // events free for reuse
+  struct Rec {
+    int id;
+    cudaEvent_t a, b;
+  };
+  std::vector<Rec> recs;
+  cudaEvent_t pending[K_COUNT] = {};
+};
+TimingState g_timing;
+
+cudaEvent_t timing_event() {
+  if (!g_timing.pool.empty()) {
+    cudaEvent_t e = g_timing.pool.back();
+    g_timing.pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
 std::atomic<int> g_algo{PC2D_ALGO_AUTO};
 std::mutex g_status_mutex;
 int *g_status_ptrs[64] = {nullptr};
@@ -26,6 +54,21 @@ void set_last_error(const char *fmt, ...) {
   va_start(ap, fmt);
   vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
   va_end(ap);
+}
+
+void timing_begin(KernelId id, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(g_timing.mu);
+  if (!g_timing.on) return;
+  cudaEvent_t e = timing_event();
+  if (e && cudaEventRecord(e, stream) == cudaSuccess) g_timing.pending[id] = e;
+}
+
+void timing_end(KernelId id, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(g_timing.mu);
+  if (!g_timing.on || !g_timing.pending[id]) return;
+  cudaEvent_t e = timing_event();
+  if (e && cudaEventRecord(e, stream) == cudaSuccess) g_timing.recs.push_back({(int)id, g_timing.pending[id], e});
+  g_timing.pending[id] = nullptr;
 }
 
 int *device_status_ptr() {
@@ -225,6 +268,47 @@ const char *pc2d_status_string(int status) {
 
 const char *pc2d_last_error(void) { return t_last_error; }
 
+int pc2d_timing_enable(int on) {
+  std::lock_guard<std::mutex> lock(g_timing.mu);
+  g_timing.on = on != 0;
+  return PC2D_OK;
+}
+
+int pc2d_timing_reset(void) {
+  std::lock_guard<std::mutex> lock(g_timing.mu);
+  for (auto &r : g_timing.recs) {
+    cudaEventSynchronize(r.b);
+    g_timing.pool.push_back(r.a);
+    g_timing.pool.push_back(r.b);
+  }
+  g_timing.recs.clear();
+  return PC2D_OK;
+}
+
+int pc2d_timing_read(const char *kernel, double *total_ms, int *launches) {
+  int id = -1;
+  for (int i = 0; i < K_COUNT; ++i)
+    if (kernel && std::strcmp(kernel, kKernelNames[i]) == 0) id = i;
+  if (id < 0 || !total_ms || !launches) {
+    set_last_error("unknown kernel family '%s'", kernel ? kernel : "(null)");
+    return PC2D_ERR_INVALID_ARGUMENT;
+  }
+  std::lock_guard<std::mutex> lock(g_timing.mu);
+  double t = 0.0;
+  int n = 0;
+  for (auto &r : g_timing.recs) {
+    if (r.id != id) continue;
+    PC2D_CUDA_CHECK(cudaEventSynchronize(r.b));
+    float ms = 0.f;
+    PC2D_CUDA_CHECK(cudaEventElapsedTime(&ms, r.a, r.b));
+    t += ms;
+    ++n;
+  }
+  *total_ms = t;
+  *launches = n;
+  return PC2D_OK;
+}
+
 int pc2d_device_status(void) {
   PC2D_CUDA_CHECK(cudaDeviceSynchronize());
   int v = 0;
@@ -240,13 +324,13 @@ int pc2d_clear_device_status(void) {
   return PC2D_OK;
 }
 
-int pc2d_selftest_bounded_wait(unsigned int max_polls, void *stream) {
+int pc2d_selftest_bounded_wait(unsigned int timeout_us, void *stream) {
   int *status = device_status_ptr();
   if (!status) {
     set_last_error("no device status word");
     return PC2D_ERR_CUDA;
   }
-  return tc_selftest_bounded_wait(max_polls, status, reinterpret_cast<cudaStream_t>(stream));
+  return tc_selftest_bounded_wait(timeout_us, status, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -59,6 +59,12 @@ __device__ __forceinline__ void record_device_error(int *status, int code) { ato
 // Host-side error message of the last failing ABI call on this thread.
 void set_last_error(const char *fmt, ...);
 
+// Optional per-kernel timing (pc2d_timing_*): brackets a launch with CUDA
+// events when enabled.  Kernel families are indexed by KernelId.
+enum KernelId { K_FORWARD = 0, K_DGRAD, K_WGRAD, K_SIMT_FORWARD, K_SIMT_DGRAD, K_SIMT_WGRAD, K_COUNT };
+void timing_begin(KernelId id, cudaStream_t stream);
+void timing_end(KernelId id, cudaStream_t stream);
+
 // Launchers implemented by the kernel translation units.
 template <typename T>
 int simt_forward(const Problem &p, const T *x, const T *pars, double factor, T *out, T *hsum,

@@ -451,7 +451,9 @@ int simt_forward(const Problem &p, const T *x, const T *pars, double factor, T *
     set_last_error("too many output channels for the CUDA-core forward (m=%d)", p.m);
     return PC2D_ERR_UNSUPPORTED;
   }
+  timing_begin(K_SIMT_FORWARD, stream);
   simt_forward_kernel<T><<<grid, kThreads, 0, stream>>>(x, pars, (T)factor, p, out, hsum);
+  timing_end(K_SIMT_FORWARD, stream);
   PC2D_LAUNCH_CHECK("simt_forward_kernel");
   return PC2D_OK;
 }
@@ -475,7 +477,9 @@ int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, co
     if (p.NHW > 0) PC2D_CUDA_CHECK(cudaMemsetAsync(dx, 0, sizeof(T) * (size_t)p.NHW * p.C, stream));
   } else {
     const dim3 grid(ceil_div(p.NHW, DM), ceil_div(p.C, DC));
+    timing_begin(K_SIMT_DGRAD, stream);
     simt_dgrad_kernel<T><<<grid, kThreads, 0, stream>>>(grad, x, pars, hsum, p, dx);
+    timing_end(K_SIMT_DGRAD, stream);
     PC2D_LAUNCH_CHECK("simt_dgrad_kernel");
   }
   if (npars == 0 || skip_wgrad) return PC2D_OK;
@@ -494,7 +498,9 @@ int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, co
   int64_t pix_per_split = (p.NPQ + splits - 1) / splits;
   pix_per_split = (pix_per_split + WP - 1) / WP * WP;
   const dim3 grid(ceil_div(p.d, WK), ceil_div(p.m, WJ), splits);
+  timing_begin(K_SIMT_WGRAD, stream);
   simt_wgrad_kernel<T><<<grid, kThreads, 0, stream>>>(grad, x, hsum, p, pix_per_split, part, sums);
+  timing_end(K_SIMT_WGRAD, stream);
   PC2D_LAUNCH_CHECK("simt_wgrad_kernel");
   const dim3 fgrid(ceil_div(p.d, kThreads), p.m);
   simt_wgrad_finalize_kernel<T><<<fgrid, kThreads, 0, stream>>>(part, sums, splits, pars, p, 2.0 * (double)(T)factor, dpars);

@@ -450,7 +450,9 @@ int launch_dgrad(const Problem &p, const DgCfg &c, const float *grad, const floa
     }
   }
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
+  timing_begin(K_DGRAD, stream);
   tc_dgrad_kernel<NC><<<grid, kThreads, dg_smem_bytes(c), stream>>>(grad, x, hsum, wsB, p, c, dx, status);
+  timing_end(K_DGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_dgrad_kernel");
   return PC2D_OK;
 }

@@ -540,8 +540,10 @@ int launch_forward(const Problem &p, const FwdCfg &c, const float *x, const floa
     }
   }
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
+  timing_begin(K_FORWARD, stream);
   tc_forward_kernel<NB><<<grid, kFwdThreads, fwd_smem_bytes(p, c), stream>>>(x, pars, wsB, cj, factor, p, c, out, hsum,
                                                                           status);
+  timing_end(K_FORWARD, stream);
   PC2D_LAUNCH_CHECK("tc_forward_kernel");
   return PC2D_OK;
 }

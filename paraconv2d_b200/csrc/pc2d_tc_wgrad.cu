@@ -444,7 +444,9 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
     }
   }
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
+  timing_begin(K_WGRAD, stream);
   tc_wgrad_kernel<<<grid, kThreads, wg_smem_bytes(c), stream>>>(grad, x, hsum, p, c, part, sums, status);
+  timing_end(K_WGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
   const dim3 fgrid(ceil_div(p.d, 256), p.m);
   tc_wgrad_finalize<<<fgrid, 256, 0, stream>>>(part, sums, pars, p, c, 2.0 * (double)(float)factor, dpars);
