@@ -92,6 +92,23 @@ int pc2d_forward(int dtype, const void *input, const void *pars, double factor,
                  int n, int channels, int height, int width, int m,
                  void *output, void *hsum, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Forward pass that allocates nothing and takes no workspace.  It has no
+ * counterpart in the reference.  It is meant for callers that may not
+ * allocate device memory while the op runs, such as plugin interfaces that
+ * pass an operator only its input and output buffers, or real-time code with
+ * a fixed memory budget: cudaMalloc can synchronise the device or fail, and
+ * those hosts forbid it.  The scratch lives in a static 8 MiB device array
+ * that every GPU loading the library keeps until exit.  Problems needing more
+ * scratch than that fail with PC2D_ERR_WORKSPACE.  The first call on a device
+ * resolves the array's address with cudaGetSymbolAddress, so make that first
+ * call before any stream capture.  All calls share the array: calls that
+ * overlap on the GPU race and must be serialised by the caller.  Arguments,
+ * results and the other errors are those of pc2d_forward. */
+int pc2d_forward_noalloc(int dtype, const void *input, const void *pars, double factor,
+                         int k0, int k1, int s0, int s1, int dl0, int dl1,
+                         int n, int channels, int height, int width, int m,
+                         void *output, void *hsum, void *stream);
+
 /* Scratch bytes pc2d_backward needs for this problem. */
 size_t pc2d_backward_workspace_size(int dtype, int n, int channels, int height, int width, int m,
                                     int k0, int k1, int s0, int s1, int dl0, int dl1,
