@@ -470,10 +470,127 @@ def launches_per_step(lib, ktimes, steps):
     return total // max(1, steps)
 
 
+def run_stack(args):
+    """Data-parallel training step of a multi-layer stack (the c5 workload:
+    3->32->64->64->64, k3 p1, stride 2 on layers 2-3, 64x64 input, global batch
+    1024, loss = sum(out^2)).  The global batch is split across the ranks
+    (strong scaling); one bucketed NCCL all-reduce (SUM) of all parameter
+    gradients per step."""
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    import paraconv2d_b200 as pc
+    from paraconv2d_b200 import _lib, workloads
+    from paraconv2d_b200.dp import GradAllReduce, shard
+
+    wl = workloads.WORKLOADS[args.workload]
+    lib = _lib.cabi()
+    x, pars, _ = workloads.draw(wl)
+    xs = shard(x, rank, world).contiguous()
+    layers = []
+    for L, pr in zip(wl.layers, pars):
+        m = pc.ParaConv2d(L.cin, L.cout, L.k, stride=L.s, padding=L.p).to(dev)
+        with torch.no_grad():
+            m.pars.copy_(pr.to(dev))
+        layers.append(m)
+    model = torch.nn.Sequential(*layers)
+    reducer = GradAllReduce(model.parameters()) if world > 1 else None
+    xd = xs.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(inp):
+        for prm in model.parameters():
+            prm.grad = None
+        y = model(inp)
+        (y * y).sum().backward()
+        if reducer is not None:
+            reducer()
+
+    def max_over_ranks(v):
+        if pg is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step(xd)
+    torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    lib.pc2d_timing_reset()
+    lib.pc2d_timing_enable(1)
+    clk = ClockSampler(local)
+    clk.__enter__()
+    tot = 0.0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.steps):
+        flush.zero_()
+        e0.record(stream)
+        step(xd)
+        e1.record(stream)
+        e1.synchronize()
+        tot += e0.elapsed_time(e1) / 1e3
+    lib.pc2d_timing_enable(0)
+    ktimes = _lib.kernel_times(KERNELS)
+    tot = max_over_ranks(tot)
+    # end to end: the shard's input from pinned host memory, gradients read back
+    x_host = xs.pin_memory()
+    grads_host = [torch.empty(prm.numel()).pin_memory() for prm in model.parameters()]
+    e_tot = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        e0.record(stream)
+        step(x_host.to(dev, non_blocking=True))
+        for gh, prm in zip(grads_host, model.parameters()):
+            gh.copy_(prm.grad, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        e_tot += e0.elapsed_time(e1) / 1e3
+    e_tot = max_over_ranks(e_tot)
+    clk.__exit__(None, None, None)
+    images = wl.n * args.steps
+    flops_img = sum(3 * workloads.fwd_flops_per_image(wl, i) for i in range(len(wl.layers)))
+    peak_3x = measure_tf32_tflops(dev) / 3.0
+    if rank == 0:
+        timed = {k: v for k, v in ktimes.items() if v[1] > 0}
+        line = {
+            "metric": f"{wl.name} data-parallel training step images/s", "value": images / tot, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded)",
+            "config": {"workload": f"{wl.name}: {wl.description}", "global_batch": wl.n,
+                       "per_gpu_batch": xs.shape[0], "parallelism": f"dp{world}",
+                       "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) before every step, outside the timed events"},
+            "e2e": {"value": images / e_tot, "unit": UNIT, "h2d_bytes_per_step": x_host.numel() * 4,
+                    "d2h_bytes_per_step": sum(g.numel() * 4 for g in grads_host)},
+            "tensor_frac_of_step": flops_img * wl.n / (tot / args.steps) / 1e12 / peak_3x / world,
+            "kernel_ms_per_step": {k: v[0] / args.steps for k, v in timed.items()},
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    from paraconv2d_b200 import workloads
+    if len(workloads.WORKLOADS[args.workload].layers) > 1:
+        return run_stack(args)
     return run_ours(args)
 
 

@@ -1,0 +1,85 @@
+"""Data-parallel training of ParaConv2d layers: one process per GPU, the batch
+split across ranks, the parameter gradients summed with one NCCL all-reduce.
+
+The global loss of a ParaConv2d stack is a sum over images, so the gradient
+of the full batch is the SUM of the ranks' gradients (not the mean that
+DistributedDataParallel takes).  Every rank draws or receives the same
+global batch and keeps its own contiguous shard, so the result does not
+depend on the number of ranks.
+"""
+from __future__ import annotations
+
+from typing import Iterable, List, Optional
+
+import torch
+import torch.distributed as dist
+
+
+def shard_bounds(n: int, rank: int, world: int):
+    """[start, stop) of rank's contiguous shard of n items (sizes differ by at most one)."""
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def shard(batch: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Rank's contiguous shard of the leading (batch) dimension."""
+    a, b = shard_bounds(batch.shape[0], rank, world)
+    return batch[a:b]
+
+
+class GradAllReduce:
+    """Sums the gradients of `params` across the ranks of `group`.
+
+    ``bucketed=True`` (default) flattens all gradients into one buffer and
+    issues a single all-reduce per step: for a 4-layer 3->32->64->64->64 stack
+    that is 186,496 floats, far below the size where splitting pays on
+    NVLink.  ``bucketed=False`` issues one asynchronous all-reduce per
+    parameter as soon as its gradient is accumulated (overlapping the
+    remaining backward); ``wait()`` completes them."""
+
+    def __init__(self, params: Iterable[torch.nn.Parameter], group: Optional[dist.ProcessGroup] = None,
+                 bucketed: bool = True):
+        self.params: List[torch.nn.Parameter] = [p for p in params if p.requires_grad]
+        self.group = group
+        self.bucketed = bucketed
+        self._works = []
+        self._hooks = []
+        self._flat = None
+        if not bucketed:
+            for p in self.params:
+                self._hooks.append(p.register_post_accumulate_grad_hook(self._on_grad))
+
+    def _on_grad(self, p):
+        self._works.append(dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+
+    def __call__(self):
+        """Call after backward: completes the sum of every gradient."""
+        if not self.bucketed:
+            self.wait()
+            return
+        grads = [p.grad for p in self.params if p.grad is not None]
+        if not grads:
+            return
+        total = sum(g.numel() for g in grads)
+        if self._flat is None or self._flat.numel() != total or self._flat.device != grads[0].device:
+            self._flat = torch.empty(total, dtype=grads[0].dtype, device=grads[0].device)
+        off = 0
+        for g in grads:
+            self._flat[off:off + g.numel()].copy_(g.reshape(-1))
+            off += g.numel()
+        dist.all_reduce(self._flat, op=dist.ReduceOp.SUM, group=self.group)
+        off = 0
+        for g in grads:
+            g.copy_(self._flat[off:off + g.numel()].view_as(g))
+            off += g.numel()
+
+    def wait(self):
+        for w in self._works:
+            w.wait()
+        self._works.clear()
+
+    def remove(self):
+        for h in self._hooks:
+            h.remove()
+        self._hooks.clear()
