@@ -496,8 +496,10 @@ def run_stack(args):
     x, pars, _ = workloads.draw(wl)
     xs = shard(x, rank, world).contiguous()
     layers = []
-    for L, pr in zip(wl.layers, pars):
-        m = pc.ParaConv2d(L.cin, L.cout, L.k, stride=L.s, padding=L.p).to(dev)
+    for i, (L, pr) in enumerate(zip(wl.layers, pars)):
+        # the first layer's input needs no gradient: skip_input_grad, as the
+        # reference module documents for the first layer of a network
+        m = pc.ParaConv2d(L.cin, L.cout, L.k, stride=L.s, padding=L.p, skip_input_grad=(i == 0)).to(dev)
         with torch.no_grad():
             m.pars.copy_(pr.to(dev))
         layers.append(m)
@@ -559,7 +561,7 @@ def run_stack(args):
     e_tot = max_over_ranks(e_tot)
     clk.__exit__(None, None, None)
     images = wl.n * args.steps
-    flops_img = sum(3 * workloads.fwd_flops_per_image(wl, i) for i in range(len(wl.layers)))
+    flops_img = sum((2 if i == 0 else 3) * workloads.fwd_flops_per_image(wl, i) for i in range(len(wl.layers)))
     peak_3x = measure_tf32_tflops(dev) / 3.0
     if rank == 0:
         timed = {k: v for k, v in ktimes.items() if v[1] > 0}

@@ -16,10 +16,12 @@
 //   - four A-producer warps (one TMEM lane = one row r) load the 32 values
 //     of their row with vector loads, form g*hsum or g, accumulate the row
 //     sum, split into tf32 hi + lo and tcgen05.st them into TMEM;
+//   - a loader warp stages the input rows the chunk's windows read (one
+//     16-byte-rounded bulk copy per channel of the window range);
 //   - eight B-producer warps (one lane = one pixel of the chunk) gather the
-//     flipped windows of the chunk's pixels (coalesced across the pixels of a
-//     warp), split them and store rows k of the 128-byte-swizzled K-major B
-//     operand in shared memory;
+//     flipped windows of the chunk's pixels from those rows, split them and
+//     store rows k of the 128-byte-swizzled K-major B operand in shared
+//     memory;
 //   - the MMA thread issues Ahi*Bhi + Alo*Bhi + Ahi*Blo (N = NR) per 8
 //     pixels.
 // At the end of a segment the epilogue warps drain the fp32 accumulator to a
@@ -28,9 +30,10 @@
 // kernel sums the slices in a fixed order in fp64 and applies the epilogue
 // above.  No floating-point atomics: the result is deterministic.
 //
-// Warp roles (544 threads, one CTA per SM): warps 0-3 A producers, 4-11 B
-// producers, 12-15 epilogue, 16 MMA issuer and TMEM owner.  All waits are
-// bounded as in the forward kernel.
+// Warp roles (576 threads, one CTA per SM): warps 0-3 A producers, 4-11 B
+// producers, 12-15 epilogue, 16 MMA issuer and TMEM owner, 17 loader of the
+// input rows the B producers gather from.  All waits are bounded as in the
+// forward kernel.
 #include <algorithm>
 #include <mutex>
 
@@ -47,7 +50,7 @@ using tc::warp_wait;
 constexpr int kChunk = 32;        // pixels per K chunk
 constexpr int kStages = 3;
 constexpr int kMaxSeg = 32;       // chunks per segment
-constexpr int kThreads = 544;
+constexpr int kThreads = 576;
 constexpr int kBWarps = 8;
 constexpr int kMinSmem = 120 * 1024;
 constexpr int kSmemLimit = 227 * 1024;
@@ -62,6 +65,10 @@ struct WgCfg {
   int64_t nseg;
   int64_t items;    // nseg * nNR * nmb
   uint32_t bstage;  // B bytes per stage (hi + lo)
+  int halo;         // 1: B rows gathered from input rows staged in shared memory
+  int nchm;         // channels a window-row range touches at most
+  int PSw;          // staged plane stride (floats, multiple of 4)
+  uint32_t hstage;  // halo bytes per stage (multiple of 1024)
 };
 
 WgCfg wg_cfg(const Problem &p, int sms) {
@@ -78,12 +85,43 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   c.nseg = (c.chunks + c.SEG - 1) / c.SEG;
   c.items = c.nseg * per;
   c.bstage = (uint32_t)(2 * c.NR * 128);
+  c.nchm = 0;
+  for (int nr = 0; nr < c.nNR; ++nr) {
+    const int64_t k0 = (int64_t)nr * c.NR, k1 = std::min<int64_t>(k0 + c.NR, p.d) - 1;
+    c.nchm = std::max(c.nchm, (int)(k1 / p.T - k0 / p.T + 1));
+  }
+  const int orow = std::min<int64_t>(p.P, (p.Q + kChunk - 2) / p.Q + 1);
+  const int rows = (orow - 1) * p.s0 + (p.k0 - 1) * p.dl0 + 1;
+  c.PSw = (int)(((int64_t)rows * p.W + 8 + 3) / 4 * 4);
+  c.hstage = (uint32_t)align_up((size_t)c.nchm * c.PSw * 4, 1024);
+  c.halo = c.nchm <= 64 ? 1 : 0;
+  const size_t need = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256) * 4 + 16 * 8 + 64;
+  if (need > (size_t)kSmemLimit) c.halo = 0;  // gather from global memory instead
+  if (!c.halo) c.hstage = 0;
   return c;
 }
 
 inline size_t wg_smem_bytes(const WgCfg &c) {
-  size_t s = 1024 + (size_t)kStages * c.bstage + 16 * 8 + 64;
+  size_t s = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * 64 * 4 + (size_t)kStages * 256 * 4 +
+             16 * 8 + 64;
   return std::max<size_t>(s, kMinSmem);
+}
+
+// Halo geometry of one 32-pixel chunk: image, first input row, input rows.
+struct ChunkGeo {
+  int64_t n;
+  int pq0, npx, ir0, rows;
+};
+
+__device__ __forceinline__ ChunkGeo chunk_geo(const Problem &p, const WgCfg &c, int64_t gc) {
+  ChunkGeo g;
+  g.n = gc / c.cpi;
+  g.pq0 = (int)(gc - g.n * c.cpi) * kChunk;
+  g.npx = min(kChunk, (int)p.PQ - g.pq0);
+  const int oya = g.pq0 / p.Q, oyb = (g.pq0 + g.npx - 1) / p.Q;
+  g.ir0 = oya * p.s0;
+  g.rows = (oyb - oya) * p.s0 + (p.k0 - 1) * p.dl0 + 1;
+  return g;
 }
 inline size_t wg_part_bytes(const WgCfg &c) { return align_up((size_t)c.items * 128 * c.NR * 4, 256); }
 inline size_t wg_sums_bytes(const WgCfg &c) { return align_up((size_t)c.items * 128 * 4, 256); }
@@ -98,11 +136,15 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  uint8_t *sB = base;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(base + (size_t)kStages * c.bstage);
+  uint8_t *sB = base;                                                  // kStages x bstage
+  uint8_t *sH = base + (size_t)kStages * c.bstage;                     // kStages x hstage
+  int *lead = reinterpret_cast<int *>(sH + (size_t)kStages * c.hstage);  // [kStages][64]
+  int *roffs = lead + kStages * 64;                                    // [kStages][256]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(roffs + kStages * 256);
   uint64_t *a_full = bars, *a_empty = bars + 3, *b_full = bars + 6, *b_empty = bars + 9;
   uint64_t *d_full = bars + 12, *d_empty = bars + 13, *final_bar = bars + 14;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 15);
+  uint64_t *h_full = bars + 15, *h_empty = bars + 18;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 21);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   if (threadIdx.x == 0) {
@@ -111,6 +153,8 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       mbar_init(&a_empty[i], 1);
       mbar_init(&b_full[i], kBWarps);
       mbar_init(&b_empty[i], 1);
+      mbar_init(&h_full[i], 1);
+      mbar_init(&h_empty[i], kBWarps);
     }
     mbar_init(d_full, 1);
     mbar_init(d_empty, 128);
@@ -213,16 +257,20 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     }
   } else if (warp < 4 + kBWarps) {
     // -------------------------------------------------------- B producers
-    // Warp bw builds rows kl = bw + 8*i of each chunk's B tile; lane i holds
-    // the input offset of row bw + 8*i of the item's window range.
+    // Warp bw builds rows kl = bw + 8*i of each chunk's B tile (lane = pixel).
+    // With c.halo the window values come from the input rows the loader warp
+    // staged in shared memory (per-row offsets in roffs[stage]); otherwise
+    // they are gathered from global memory (lane i holds the input offset of
+    // row bw + 8*i of the item's window range).
     const int bw = warp - 4;
     const int nrows = (c.NR - bw + kBWarps - 1) / kBWarps;  // <= 32
+    const uint32_t cpos = (uint32_t)(lane & 3) * 4;
     uint32_t it = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
       const int64_t seg = item / per;
       const int nr = (int)((item - seg * per) / c.nmb);
       int myoff = -1;
-      {
+      if (!c.halo) {
         const int kl = bw + kBWarps * lane;
         const int64_t k = (int64_t)nr * c.NR + kl;
         if (kl < c.NR && k < p.d) {
@@ -232,30 +280,41 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       }
       const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
       for (int64_t gc = g0; gc < g1; ++gc, ++it) {
-        const int64_t n = gc / c.cpi;
-        const int pq = (int)(gc - n * c.cpi) * kChunk + lane;
-        const bool pvalid = pq < p.PQ;
-        int64_t pbase = 0;
-        if (pvalid) {
-          const int oy = pq / p.Q, ox = pq - (pq / p.Q) * p.Q;
-          pbase = n * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
-        }
+        const ChunkGeo cg = chunk_geo(p, c, gc);
+        const int pq = cg.pq0 + lane;
+        const bool pvalid = lane < cg.npx;
+        const int oy = pq / p.Q, ox = pq - (pq / p.Q) * p.Q;
         const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (c.halo && !warp_wait(&h_full[st], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
         if (!warp_wait(&b_empty[st], ph ^ 1, abort_flag)) {
           ok = false;
           break;
         }
         uint8_t *stg = sB + (size_t)st * c.bstage;
-        const uint32_t cpos = (uint32_t)(lane & 3) * 4;
-        for (int i0 = 0; i0 < nrows; i0 += 4) {
-          float v[4];
+        const float *halo = reinterpret_cast<const float *>(sH + (size_t)st * c.hstage);
+        const int *ro = roffs + st * 256;
+        const int poff = (oy * p.s0 - cg.ir0) * p.W + ox * p.s1;
+        const int64_t pbase = cg.n * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
+        for (int i0 = 0; i0 < nrows; i0 += 8) {
+          float v[8];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int o = __shfl_sync(0xffffffffu, myoff, (i0 + u) & 31);
-            v[u] = (i0 + u < nrows && pvalid && o >= 0) ? __ldg(x + pbase + o) : 0.f;
+          for (int u = 0; u < 8; ++u) {
+            const int kl = bw + kBWarps * (i0 + u);
+            float a = 0.f;
+            if (c.halo) {
+              const int o = (i0 + u < nrows) ? ro[kl] : -1;
+              if (pvalid && o >= 0) a = halo[o + poff];
+            } else {
+              const int o = __shfl_sync(0xffffffffu, myoff, (i0 + u) & 31);
+              if (i0 + u < nrows && pvalid && o >= 0) a = __ldg(x + pbase + o);
+            }
+            v[u] = a;
           }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 8; ++u) {
             if (i0 + u < nrows) {
               const uint32_t kl = (uint32_t)(bw + kBWarps * (i0 + u));
               const uint32_t hb = tf32_hi_bits(v[u]);
@@ -267,7 +326,10 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&b_full[st]);
+        if (lane == 0) {
+          mbar_arrive(&b_full[st]);
+          if (c.halo) mbar_arrive(&h_empty[st]);
+        }
       }
     }
   } else if (warp < 16) {
@@ -296,6 +358,76 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       }
       tc_fence_before();
       mbar_arrive(d_empty);
+    }
+  } else if (warp == 17) {
+    // -------------------------------------------------------------- loader
+    // Stages, per chunk, the input rows its windows read for the channels of
+    // the item's window range (one 16-byte-rounded bulk copy per channel), and
+    // the offset of every window row of the range inside that stage.
+    if (c.halo) {
+      uint32_t it = 0;
+      for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
+        const int64_t seg = item / per;
+        const int nr = (int)((item - seg * per) / c.nmb);
+        const int64_t kbase = (int64_t)nr * c.NR;
+        const int clo = (int)(kbase / p.T);
+        // (channel - clo, tap offset) of the window rows this lane writes
+        int rc[8], rt[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int kl = lane + 32 * e;
+          const int64_t k = kbase + kl;
+          rc[e] = -1;
+          rt[e] = 0;
+          if (kl < c.NR && k < p.d) {
+            const int ch = (int)(k / p.T), tap = (int)(k - (int64_t)ch * p.T);
+            rc[e] = ch - clo;
+            rt[e] = tap_row(p, tap) * p.W + tap_col(p, tap);
+          }
+        }
+        const int nch = (int)(std::min<int64_t>(kbase + c.NR, p.d) - 1) / p.T - clo + 1;
+        const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
+        for (int64_t gc = g0; gc < g1; ++gc, ++it) {
+          const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+          if (!warp_wait(&h_empty[st], ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const ChunkGeo cg = chunk_geo(p, c, gc);
+          const float *xrow = x + cg.n * p.CHW + (int64_t)cg.ir0 * p.W;
+          const int64_t run = (int64_t)cg.rows * p.W;
+          uint32_t bytes = 0;
+          for (int ci = lane; ci < nch; ci += 32) {
+            const tc::BulkSpan sp = tc::bulk_span(xrow + (int64_t)(clo + ci) * p.HW, run);
+            lead[st * 64 + ci] = sp.lead;
+            bytes += sp.bytes;
+          }
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
+          __syncwarp();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int kl = lane + 32 * e;
+            if (kl < c.NR)
+              roffs[st * 256 + kl] = rc[e] >= 0 ? rc[e] * c.PSw + lead[st * 64 + rc[e]] + rt[e] : -1;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive_expect_tx(&h_full[st], bytes);
+          __syncwarp();
+          uint8_t *hb = sH + (size_t)st * c.hstage;
+          for (int ci = lane; ci < nch; ci += 32) {
+            const tc::BulkSpan sp = tc::bulk_span(xrow + (int64_t)(clo + ci) * p.HW, run);
+            bulk_g2s(hb + (size_t)ci * c.PSw * 4, sp.src, sp.bytes, &h_full[st]);
+          }
+          __syncwarp();
+        }
+      }
+      // Drain: the copies issued last have landed before the CTA exits.
+      const uint32_t last = it < (uint32_t)kStages ? it : (uint32_t)kStages;
+      for (uint32_t i = 0; i < last; ++i) {
+        const uint32_t idx = it - 1 - i;
+        mbar_wait(&h_full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
+      }
     }
   } else {
     // ---------------------------------------------------------------- MMA

@@ -68,7 +68,7 @@ def test_module_forward_backward(kw):
 def test_module_fp16_input():
     m = _module(3, 8, 3, padding=1)
     x = (torch.rand(2, 3, 8, 8) * 2 - 1).half()
-    y = m(x.cuda())
+    y = m(x.cuda()).detach()
     assert y.dtype == torch.float16
     out, _ = _oracle_layer(m, x.float())
     assert np.allclose(y.float().cpu().numpy(), out, rtol=1e-2, atol=1e-2)
