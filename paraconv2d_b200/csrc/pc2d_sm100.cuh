@@ -82,6 +82,11 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, u
       : "memory");
 }
 
+// Hint: bring the line holding `p` into L2 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // 4-byte asynchronous copy global -> shared (LDGSTS).  With valid == false no
 // global byte is read and the destination is zero-filled.
 __device__ __forceinline__ void cp_async4(void *smem_dst, const void *gmem_src, bool valid) {

@@ -8,7 +8,10 @@
 //                    - x[c,y,x] * SG[y,x]),   SG = sum_{tap,j} g[j,o(tap)]
 // is an implicit GEMM with M = 128 input pixels of one image per tile,
 // N = input channels of a block (NC <= 64) and K = (j-block of 16 output
-// channels, tap, j, {g*hsum, g}) swept 32 at a time.  The windows are flipped
+// channels, tap, j, {g*hsum, g}) swept 32 at a time.  With stride s > 1 only
+// the taps whose row/column offset has the residue of (y, x) mod s reach an
+// input pixel, so the tiles group pixels by stride phase (y mod s0, x mod s1)
+// and K runs over that phase's taps only (a quarter of them for stride 2).  The windows are flipped
 // exactly as in the forward pass: tap (ix2, iy2) of output pixel (oy, ox)
 // reads input (oy*s0 + (k0-1-ix2)*dl0, ox*s1 + (k1-1-iy2)*dl1).
 //
@@ -55,18 +58,48 @@ constexpr int kMinSmem = 120 * 1024;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr uint32_t kColA = 256;
 
+constexpr int kMaxPh = 16;  // stride phases s0*s1
+constexpr int kMaxKs = 32;  // kernel extent per axis
+
 struct DgCfg {
   int ncb;          // input-channel blocks
   int NC;           // channels per block (multiple of 16, <= 64)
   int nJB;          // j-blocks
-  int nK;           // stages per tile = nJB * T
-  int nGroups;      // partial sums per tile
-  int tpi;          // tiles per image
+  int nK;           // weight stages of the prep layout = nJB * T
+  int nph;          // stride phases (y mod s0, x mod s1)
+  int ph_rows[kMaxPh], ph_cols[kMaxPh];   // phase grid of an image
+  int ph_ntaps[kMaxPh];                   // taps that reach the phase
+  int ph_first[kMaxPh + 1];               // first tile of each phase within an image
+  int ph_tap0[kMaxPh + 1];                // first entry of each phase in the tap table
+  int tpi;          // tiles per image (all phases)
   int64_t tiles, items;
   int PSo;          // g/hsum plane stride (floats, multiple of 4)
   uint32_t bstage;  // B bytes per stage (hi + lo)
   uint32_t jslot;   // bytes of a j-block slot (32 planes), multiple of 1024
 };
+
+// Per-phase tables copied from DgCfg into shared memory at kernel start
+// (indexing a kernel parameter with a run-time index makes the compiler read
+// every field of it through generic loads).
+struct DgPhases {
+  int first[kMaxPh + 1];
+  int tap0[kMaxPh + 1];
+  int rows[kMaxPh];
+  int cols[kMaxPh];
+  int ntaps[kMaxPh];
+};
+
+// Taps that reach input rows y with y % s0 == py: tap row (k0-1-ix2)*dl0 must
+// have the same residue (the output pixel is then (y - row)/s0 exactly).
+inline int phase_rows(int k, int dl, int s, int py, int *list) {
+  int n = 0;
+  for (int i = 0; i < k; ++i)
+    if (((k - 1 - i) * dl) % s == py) {
+      if (list) list[n] = i;
+      ++n;
+    }
+  return n;
+}
 
 DgCfg dg_cfg(const Problem &p) {
   DgCfg c;
@@ -75,12 +108,35 @@ DgCfg dg_cfg(const Problem &p) {
   c.NC = (nc + 15) / 16 * 16;
   c.nJB = ceil_div(p.m, kJB);
   c.nK = c.nJB * p.T;
-  c.nGroups = ceil_div(c.nK, kGroupStages);
-  c.tpi = ceil_div(p.HW, kTileM);
+  c.nph = p.s0 * p.s1;
+  int orows = 1;
+  c.tpi = 0;
+  for (int ph = 0; ph < kMaxPh; ++ph) {
+    c.ph_rows[ph] = c.ph_cols[ph] = c.ph_ntaps[ph] = 0;
+    c.ph_first[ph] = 0;
+    c.ph_tap0[ph] = 0;
+  }
+  int taps = 0;
+  for (int ph = 0; ph < c.nph && ph < kMaxPh; ++ph) {
+    const int py = ph / p.s1, px = ph % p.s1;
+    c.ph_rows[ph] = p.H > py ? (p.H - py + p.s0 - 1) / p.s0 : 0;
+    c.ph_cols[ph] = p.W > px ? (p.W - px + p.s1 - 1) / p.s1 : 0;
+    c.ph_ntaps[ph] = phase_rows(p.k0, p.dl0, p.s0, py, nullptr) * phase_rows(p.k1, p.dl1, p.s1, px, nullptr);
+    c.ph_first[ph] = c.tpi;
+    c.ph_tap0[ph] = taps;
+    taps += c.ph_ntaps[ph];
+    const int64_t npix = (int64_t)c.ph_rows[ph] * c.ph_cols[ph];
+    c.tpi += (int)((npix + kTileM - 1) / kTileM);
+    if (c.ph_cols[ph] > 0) {
+      const int span = (int)std::min<int64_t>(c.ph_rows[ph], (c.ph_cols[ph] + kTileM - 2) / c.ph_cols[ph] + 1);
+      const int yspan = (span - 1) * p.s0 + 1;
+      orows = std::max(orows, std::min<int>(p.P, (yspan - 1 + (p.k0 - 1) * p.dl0) / p.s0 + 2));
+    }
+  }
+  c.ph_first[std::min(c.nph, kMaxPh)] = c.tpi;
+  c.ph_tap0[std::min(c.nph, kMaxPh)] = taps;
   c.tiles = (int64_t)p.n * c.tpi;
   c.items = c.tiles * c.ncb;
-  const int irows = std::min<int64_t>(p.H, (p.W + kTileM - 2) / p.W + 1);
-  const int orows = std::min<int>(p.P, (irows - 1 + (p.k0 - 1) * p.dl0) / p.s0 + 2);
   c.PSo = (int)(((int64_t)orows * p.Q + 8 + 3) / 4 * 4);
   c.bstage = (uint32_t)(2 * c.NC * 128);
   c.jslot = (uint32_t)align_up((size_t)2 * kJB * c.PSo * 4, 1024);
@@ -89,7 +145,9 @@ DgCfg dg_cfg(const Problem &p) {
 
 inline size_t dg_bsplit_bytes(const DgCfg &c) { return (size_t)c.ncb * c.nK * c.bstage; }
 inline size_t dg_smem_bytes(const DgCfg &c) {
-  size_t s = 1024 + (size_t)kStages * c.bstage + 2 * (size_t)c.jslot + 2 * 2 * kJB * 4 + 2 * kTileM * 4 + 24 * 8 + 64;
+  size_t s = 1024 + (size_t)kStages * c.bstage + 2 * (size_t)c.jslot + (size_t)c.NC * kTileM * 4 +
+             2 * 2 * kJB * 4 + 2 * kTileM * 4 + 24 * 8 + 64 +
+             sizeof(DgPhases) + (size_t)(c.nK / c.nJB) * 8;
   return std::max<size_t>(s, kMinSmem);
 }
 
@@ -118,23 +176,60 @@ __global__ void tc_dg_prep_weights(const float *__restrict__ pars, Problem p, Dg
 
 struct DgGeo {
   int64_t n;
-  int q0;      // first input pixel of the tile (within the image)
-  int oylo;    // first output row staged
-  int orows;   // output rows staged (may be 0)
+  int ph, py, px;  // stride phase
+  int q0;          // first phase-grid pixel of the tile
+  int cols, npix;  // phase grid width and size
+  int oylo;        // first output row staged
+  int orows;       // output rows staged (may be 0)
+  int ntaps;       // taps reaching this phase
+  int tap0;        // the phase's first entry in the tap table
 };
 
-__device__ __forceinline__ DgGeo dg_geo(const Problem &p, const DgCfg &c, int64_t t) {
+__device__ __forceinline__ DgGeo dg_geo(const Problem &p, const DgCfg &c, const DgPhases &ps, int64_t t) {
   DgGeo g;
   g.n = t / c.tpi;
-  g.q0 = (int)(t - g.n * c.tpi) * kTileM;
-  const int qlast = min(g.q0 + kTileM - 1, (int)p.HW - 1);
-  const int iya = g.q0 / p.W, iyb = qlast / p.W;
-  const int lo = iya - (p.k0 - 1) * p.dl0;
-  int oylo = lo <= 0 ? 0 : (lo + p.s0 - 1) / p.s0;
-  int oyhi = min(p.P - 1, iyb / p.s0);
+  const int r = (int)(t - g.n * c.tpi);
+  int ph = 0;
+  while (ph + 1 < c.nph && ps.first[ph + 1] <= r) ++ph;
+  g.ph = ph;
+  g.py = ph / p.s1;
+  g.px = ph - g.py * p.s1;
+  g.q0 = (r - ps.first[ph]) * kTileM;
+  g.cols = ps.cols[ph];
+  g.npix = ps.rows[ph] * g.cols;
+  g.ntaps = ps.ntaps[ph];
+  g.tap0 = ps.tap0[ph];
+  const int qlast = min(g.q0 + kTileM - 1, g.npix - 1);
+  const int ya = g.py + p.s0 * (g.q0 / g.cols), yb = g.py + p.s0 * (qlast / g.cols);
+  const int lo = ya - (p.k0 - 1) * p.dl0;
+  const int oylo = lo <= 0 ? 0 : (lo + p.s0 - 1) / p.s0;
+  const int oyhi = min(p.P - 1, yb / p.s0);
   g.oylo = oylo;
   g.orows = oyhi >= oylo ? oyhi - oylo + 1 : 0;
   return g;
+}
+
+// Entry e of the tap table, phase by phase in K order: the tap index
+// (ix2*k1 + iy2) and, packed as (dy << 16) | dx, the output-pixel offsets of
+// the tap within the phase grid.  An input pixel at phase-grid position
+// (a, b) of phase (py, px), i.e. (y, x) = (py + s0*a, px + s1*b), receives
+// that tap from output pixel (a - dy, b - dx), because the tap's row offset
+// (k0-1-ix2)*dl0 is py + s0*dy (columns likewise).
+__device__ __forceinline__ int2 dg_tap_entry(const Problem &p, const DgCfg &c, const DgPhases &ps, int e) {
+  int ph = 0;
+  while (ph + 1 < c.nph && ps.tap0[ph + 1] <= e) ++ph;
+  const int py = ph / p.s1, px = ph - py * p.s1;
+  int ncl = 0;
+  for (int i = 0; i < p.k1; ++i) ncl += (((p.k1 - 1 - i) * p.dl1) % p.s1 == px);
+  const int ti = e - ps.tap0[ph];
+  const int ri = ti / ncl, ci = ti - ri * ncl;
+  int ix2 = 0, iy2 = 0;
+  for (int i = 0, n = 0; i < p.k0; ++i)
+    if (((p.k0 - 1 - i) * p.dl0) % p.s0 == py && n++ == ri) ix2 = i;
+  for (int i = 0, n = 0; i < p.k1; ++i)
+    if (((p.k1 - 1 - i) * p.dl1) % p.s1 == px && n++ == ci) iy2 = i;
+  const int dy = ((p.k0 - 1 - ix2) * p.dl0 - py) / p.s0, dxo = ((p.k1 - 1 - iy2) * p.dl1 - px) / p.s1;
+  return make_int2(ix2 * p.k1 + iy2, (dy << 16) | dxo);
 }
 
 template <int NC>
@@ -146,7 +241,8 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   uint8_t *sB = base;                                             // kStages x bstage
   uint8_t *sJ = base + (size_t)kStages * c.bstage;                // 2 x jslot
-  int *jtab = reinterpret_cast<int *>(sJ + 2 * (size_t)c.jslot);  // [2][32] plane offsets (-1 = zero)
+  float *sx = reinterpret_cast<float *>(sJ + 2 * (size_t)c.jslot);  // [NC][128] input values of the tile
+  int *jtab = reinterpret_cast<int *>(sx + NC * kTileM);            // [2][32] plane offsets (-1 = zero)
   float *sgbuf = reinterpret_cast<float *>(jtab + 2 * 2 * kJB);   // [2][128]
   uint64_t *bars = reinterpret_cast<uint64_t *>((reinterpret_cast<uintptr_t>(sgbuf + 2 * kTileM) + 7) & ~(uintptr_t)7);
   uint64_t *full = bars, *a_full = bars + 4, *s_empty = bars + 8;
@@ -154,7 +250,24 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   uint64_t *sg_full = bars + 20, *sg_empty = bars + 22, *final_bar = bars + 24;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 25);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  DgPhases &ps = *reinterpret_cast<DgPhases *>(tmem_holder + 2);
+  int2 *ptab = reinterpret_cast<int2 *>(&ps + 1);  // [T] tap table
 
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i <= kMaxPh; ++i) {
+      ps.first[i] = c.ph_first[i];
+      ps.tap0[i] = c.ph_tap0[i];
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxPh; ++i) {
+      ps.rows[i] = c.ph_rows[i];
+      ps.cols[i] = c.ph_cols[i];
+      ps.ntaps[i] = c.ph_ntaps[i];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < p.T; e += blockDim.x) ptab[e] = dg_tap_entry(p, c, ps, e);
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&full[i], 1);
@@ -190,10 +303,10 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     uint32_t it = 0, jit = 0;
     int64_t li = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x, ++li) {
-      const DgGeo tg = dg_geo(p, c, item / c.ncb);
+      const DgGeo tg = dg_geo(p, c, ps, item / c.ncb);
       const int q = tg.q0 + r;
-      const bool pvalid = q < p.HW;
-      const int iy = q / p.W, ix = q - (q / p.W) * p.W;
+      const bool pvalid = q < tg.npix;
+      const int ay = q / tg.cols, bx = q - ay * tg.cols;  // phase-grid position
       float sg = 0.f;
       for (int jb = 0; jb < c.nJB && ok; ++jb, ++jit) {
         const uint32_t js = jit & 1, jph = (jit >> 1) & 1;
@@ -211,22 +324,18 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           to[4 * q4 + 2] = t4.z;
           to[4 * q4 + 3] = t4.w;
         }
-        for (int tap = 0; tap < p.T; ++tap, ++it) {
+        for (int ti = 0; ti < tg.ntaps; ++ti, ++it) {
           const uint32_t st = it % kStages, ph = (it / kStages) & 1;
           if (!warp_wait(&full[st], ph, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          // output pixel whose window puts this tap on (iy, ix)
-          const int yy = iy - tap_row(p, tap), xx = ix - tap_col(p, tap);
-          bool valid = pvalid && yy >= 0 && xx >= 0;
-          int ooff = 0;
-          if (valid) {
-            const int oy = yy / p.s0, ox = xx / p.s1;
-            valid = (oy * p.s0 == yy) && (ox * p.s1 == xx) && oy < p.P && ox < p.Q;
-            ooff = (oy - tg.oylo) * p.Q + ox;
-          }
+          // output pixel whose window puts this tap on the input pixel
+          const int dyx = ptab[tg.tap0 + ti].y;
+          const int oy = ay - (dyx >> 16), ox = bx - (dyx & 0xffff);
+          const bool valid = pvalid && oy >= 0 && ox >= 0 && oy < p.P && ox < p.Q;
+          const int ooff = (oy - tg.oylo) * p.Q + ox;
           uint32_t hi[kKS], lo[kKS];
 #pragma unroll
           for (int jl = 0; jl < kJB; ++jl) {
@@ -270,10 +379,28 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x, ++li) {
       const int64_t t = item / c.ncb;
       const int cb = (int)(item - t * c.ncb);
+      const DgGeo tg = dg_geo(p, c, ps, t);
+      const int ngroups = (c.nJB * tg.ntaps + kGroupStages - 1) / kGroupStages;
+      // this pixel's input values are needed at the end of the item: copy
+      // them to shared memory now, behind the item's MMAs (each thread reads
+      // back only what it copied, so the cp.async wait alone orders them)
+      const int q = tg.q0 + r;
+      const bool pv = q < tg.npix;
+      int64_t xb = 0;
+      if (pv) {
+        const int ay = q / tg.cols;
+        xb = tg.n * p.CHW + (int64_t)(tg.py + p.s0 * ay) * p.W + tg.px + p.s1 * (q - ay * tg.cols);
+#pragma unroll 8
+        for (int cc = 0; cc < NC; ++cc) {
+          const bool have = cb * NC + cc < p.C;
+          cp_async4(sx + cc * kTileM + r, have ? x + xb + (int64_t)(cb * NC + cc) * p.HW : x, have);
+        }
+      }
+      cp_async_commit();
       float acc[NC];
 #pragma unroll
       for (int j = 0; j < NC; ++j) acc[j] = 0.f;
-      for (int gi = 0; gi < c.nGroups; ++gi, ++grp) {
+      for (int gi = 0; gi < ngroups; ++gi, ++grp) {
         const uint32_t slot = grp % kSlots, ph = (grp / kSlots) & 1;
         if (!warp_wait(&gr_full[slot], ph, abort_flag)) {
           ok = false;
@@ -303,20 +430,15 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       }
       const float sg = sgbuf[tb * kTileM + r];
       mbar_arrive(&sg_empty[tb]);
-      const int64_t nimg = t / c.tpi;
-      const int q = (int)(t - nimg * c.tpi) * kTileM + r;
-      if (q < p.HW) {
-        const int64_t xb = nimg * p.CHW + q;
+      cp_async_wait<0>();
+      if (pv) {
 #pragma unroll
-        for (int cc = 0; cc < NC; ++cc) {
-          const int ch = cb * NC + cc;
-          if (ch < p.C) {
-            const int64_t xi = xb + (int64_t)ch * p.HW;
-            dx[xi] = 2.f * (acc[cc] - __ldg(x + xi) * sg);
-          }
-        }
+        for (int cc = 0; cc < NC; ++cc)
+          if (cb * NC + cc < p.C)
+            dx[xb + (int64_t)(cb * NC + cc) * p.HW] = 2.f * (acc[cc] - sx[cc * kTileM + r] * sg);
       }
     }
+    cp_async_wait<0>();  // copies of an item left on an error path
   } else if (warp == 8) {
     // ------------------------------------------------------------- MMA
     const uint32_t id_main = idesc_tf32(kTileM, 2 * NC);
@@ -324,10 +446,12 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     const uint32_t sB_addr = smem_u32(sB);
     uint32_t it = 0, grp = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
+      const DgGeo tg = dg_geo(p, c, ps, item / c.ncb);
+      const int nk = c.nJB * tg.ntaps;
       uint32_t dcol = 0, slot = 0;
-      for (int kq = 0; kq < c.nK; ++kq, ++it) {
+      for (int kq = 0; kq < nk; ++kq, ++it) {
         const bool gstart = (kq % kGroupStages) == 0;
-        const bool gend = (kq % kGroupStages) == kGroupStages - 1 || kq == c.nK - 1;
+        const bool gend = (kq % kGroupStages) == kGroupStages - 1 || kq == nk - 1;
         if (gstart) {
           slot = grp % kSlots;
           if (!warp_wait(&gr_empty[slot], ((grp / kSlots) & 1) ^ 1, abort_flag)) {
@@ -367,7 +491,7 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
       const int64_t t = item / c.ncb;
       const int cb = (int)(item - t * c.ncb);
-      const DgGeo tg = dg_geo(p, c, t);
+      const DgGeo tg = dg_geo(p, c, ps, t);
       const int64_t run = (int64_t)tg.orows * p.Q;
       for (int jb = 0; jb < c.nJB && ok; ++jb, ++jit) {
         const uint32_t js = jit & 1, jph = (jit >> 1) & 1;
@@ -394,13 +518,14 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         if (have) bulk_g2s(sJ + (size_t)js * c.jslot + (size_t)lane * c.PSo * 4, sp.src, sp.bytes, &jfull[js]);
         __syncwarp();
         ++jissued;
-        for (int tap = 0; tap < p.T; ++tap, ++it) {
+        for (int ti = 0; ti < tg.ntaps; ++ti, ++it) {
           const uint32_t st = it % kStages, ph = (it / kStages) & 1;
           if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
             ok = false;
             break;
           }
           if (lane == 0) {
+            const int tap = ptab[tg.tap0 + ti].x;
             mbar_arrive_expect_tx(&full[st], c.bstage);
             bulk_g2s(sB + (size_t)st * c.bstage, wsB + ((int64_t)cb * c.nK + jb * p.T + tap) * 2 * c.NC * 32,
                      c.bstage, &full[st]);
@@ -459,6 +584,7 @@ int launch_dgrad(const Problem &p, const DgCfg &c, const float *grad, const floa
 
 bool dg_supported(const Problem &p) {
   if (p.NPQ <= 0 || p.m < 1 || p.HW >= ((int64_t)1 << 30) || p.PQ >= ((int64_t)1 << 30)) return false;
+  if (p.s0 * p.s1 > kMaxPh || p.k0 > kMaxKs || p.k1 > kMaxKs) return false;
   const DgCfg c = dg_cfg(p);
   return dg_smem_bytes(c) <= (size_t)kSmemLimit && c.PSo * 2 * kJB < (1 << 30);
 }
