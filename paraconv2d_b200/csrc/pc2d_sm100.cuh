@@ -82,6 +82,18 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, u
       : "memory");
 }
 
+// One lane of the (fully active) warp returns true: the lane that issues the
+// warp's tcgen05.mma / commit instructions.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Hint: bring the line holding `p` into L2 (no register result, no wait).
 __device__ __forceinline__ void prefetch_l2(const void *p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));

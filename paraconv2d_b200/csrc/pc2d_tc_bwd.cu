@@ -11,28 +11,32 @@
 // channels, tap, j, {g*hsum, g}) swept 32 at a time.  With stride s > 1 only
 // the taps whose row/column offset has the residue of (y, x) mod s reach an
 // input pixel, so the tiles group pixels by stride phase (y mod s0, x mod s1)
-// and K runs over that phase's taps only (a quarter of them for stride 2).  The windows are flipped
-// exactly as in the forward pass: tap (ix2, iy2) of output pixel (oy, ox)
+// and K runs over that phase's taps only (a quarter of them for stride 2).
+// The windows are flipped exactly as in the forward pass: tap (ix2, iy2) of output pixel (oy, ox)
 // reads input (oy*s0 + (k0-1-ix2)*dl0, ox*s1 + (k1-1-iy2)*dl1).
 //
-// Data movement:
-//   - the loader warp stages, per j-block, the rows of g and hsum the tile's
-//     windows reach (one 1-D bulk copy per output-channel plane, shared by
-//     the T taps of the j-block), and per 32-K stage the pre-split weights
-//     [W hi; W lo] (written once per call by a prep kernel);
-//   - producer warps (one TMEM lane = one input pixel) locate, per tap, the
-//     output pixel whose window covers them, form g*hsum and g for the 16
-//     channels of the stage, accumulate SG, split into tf32 hi + lo and
-//     tcgen05.st them into TMEM (A operand);
-//   - the MMA thread issues per 8-wide K step two MMAs:
+// Warp roles (352 threads):
+//   - warps 0-3, producers (one TMEM lane = one input pixel): per tap, locate
+//     the output pixel whose window covers the pixel, form g*hsum and g for
+//     the 16 channels of the stage from the staged planes, accumulate SG,
+//     split into tf32 hi + lo and tcgen05.st them into TMEM (A operand).  A
+//     producer reuses an A slot as soon as the MMAs that read it complete;
+//   - warps 4-7, epilogue: drain the partial sums (a fresh one every 64 K, in
+//     one of two TMEM slots) into fp32 registers, and write
+//     dx = 2 * (acc - x * SG), with x copied to shared memory (cp.async) at
+//     the start of the tile;
+//   - warp 8, MMA (one thread): per 8-wide K step two MMAs
 //       [main | corr] = Ahi * [W hi; W lo]   (N = 2 NC)
 //       corr         += Alo * W hi            (N = NC)
-//     so main + corr = Ahi*Bhi + Ahi*Blo + Alo*Bhi (3xTF32).
-//   - every 64 K start a fresh partial sum in one of two TMEM slots, which
-//     the epilogue warps drain into fp32 registers; the epilogue finally
-//     writes dx = 2 * (acc - x * SG).
-// Warp roles, barriers and the bounded-wait failure path are those of the
-// forward kernel (pc2d_tc_fwd.cu).
+//     so main + corr = Ahi*Bhi + Ahi*Blo + Alo*Bhi (3xTF32);
+//   - warp 9, weight loader: per 32-K stage the pre-split weights
+//     [W hi; W lo] (written once per call by a prep kernel), one bulk copy;
+//   - warp 10, plane loader: per j-block the rows of g and hsum that the
+//     tile's windows reach, one 1-D bulk copy per output-channel plane,
+//     shared by the taps of the j-block, two j-blocks in flight.
+// Every wait is bounded; on a timeout the kernel records the error, stops
+// its loops, drains its own copies and frees TMEM, as the forward kernel
+// (pc2d_tc_fwd.cu) does.
 #include <algorithm>
 #include <mutex>
 
@@ -49,11 +53,11 @@ using tc::warp_wait;
 constexpr int kTileM = 128;
 constexpr int kKS = 32;
 constexpr int kJB = 16;          // output channels per j-block (32 K per tap)
-constexpr int kStages = 4;
-constexpr int kSlots = 2;
-constexpr int kGroupStages = 2;
+constexpr int kStages = 2;       // A/B stages of kTapsPS taps (64 K) each
+constexpr int kTapsPS = 2;       // taps per stage
+constexpr int kSlots = 2;        // accumulator slots (one partial sum per stage)
 constexpr int kMaxNC = 64;
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kMinSmem = 120 * 1024;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr uint32_t kColA = 256;
@@ -138,14 +142,14 @@ DgCfg dg_cfg(const Problem &p) {
   c.tiles = (int64_t)p.n * c.tpi;
   c.items = c.tiles * c.ncb;
   c.PSo = (int)(((int64_t)orows * p.Q + 8 + 3) / 4 * 4);
-  c.bstage = (uint32_t)(2 * c.NC * 128);
+  c.bstage = (uint32_t)(2 * c.NC * 128);  // one tap
   c.jslot = (uint32_t)align_up((size_t)2 * kJB * c.PSo * 4, 1024);
   return c;
 }
 
 inline size_t dg_bsplit_bytes(const DgCfg &c) { return (size_t)c.ncb * c.nK * c.bstage; }
 inline size_t dg_smem_bytes(const DgCfg &c) {
-  size_t s = 1024 + (size_t)kStages * c.bstage + 2 * (size_t)c.jslot + (size_t)c.NC * kTileM * 4 +
+  size_t s = 1024 + (size_t)kStages * kTapsPS * c.bstage + 2 * (size_t)c.jslot + (size_t)c.NC * kTileM * 4 +
              2 * 2 * kJB * 4 + 2 * kTileM * 4 + 24 * 8 + 64 +
              sizeof(DgPhases) + (size_t)(c.nK / c.nJB) * 8;
   return std::max<size_t>(s, kMinSmem);
@@ -232,6 +236,25 @@ __device__ __forceinline__ int2 dg_tap_entry(const Problem &p, const DgCfg &c, c
   return make_int2(ix2 * p.k1 + iy2, (dy << 16) | dxo);
 }
 
+// 32 A values of one tap for this pixel: {g*hsum, g} of the j-block's 16
+// channels at the output pixel ooff of the staged planes, split into tf32
+// hi + lo; accumulates SG.
+__device__ __forceinline__ void dg_gather(const float *planes, const int (&to)[2 * kJB], bool valid, int ooff,
+                                          float &sg, uint32_t (&hi)[kKS], uint32_t (&lo)[kKS]) {
+#pragma unroll
+  for (int jl = 0; jl < kJB; ++jl) {
+    const int og = to[2 * jl], oh = to[2 * jl + 1];
+    const float gv = (valid && og >= 0) ? planes[og + ooff] : 0.f;
+    const float hv = (valid && oh >= 0) ? planes[oh + ooff] : 0.f;
+    sg += gv;
+    const float a0 = gv * hv, a1 = gv;
+    hi[2 * jl] = tf32_hi_bits(a0);
+    lo[2 * jl] = __float_as_uint(a0 - __uint_as_float(hi[2 * jl]));
+    hi[2 * jl + 1] = tf32_hi_bits(a1);
+    lo[2 * jl + 1] = __float_as_uint(a1 - __uint_as_float(hi[2 * jl + 1]));
+  }
+}
+
 template <int NC>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, const float *__restrict__ hsum,
@@ -239,16 +262,16 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  uint8_t *sB = base;                                             // kStages x bstage
-  uint8_t *sJ = base + (size_t)kStages * c.bstage;                // 2 x jslot
-  float *sx = reinterpret_cast<float *>(sJ + 2 * (size_t)c.jslot);  // [NC][128] input values of the tile
-  int *jtab = reinterpret_cast<int *>(sx + NC * kTileM);            // [2][32] plane offsets (-1 = zero)
-  float *sgbuf = reinterpret_cast<float *>(jtab + 2 * 2 * kJB);   // [2][128]
+  uint8_t *sB = base;                                                 // [kStages][kTapsPS] x bstage
+  uint8_t *sJ = base + (size_t)kStages * kTapsPS * c.bstage;          // 2 x jslot
+  float *sx = reinterpret_cast<float *>(sJ + 2 * (size_t)c.jslot);    // [NC][128] input values of the tile
+  int *jtab = reinterpret_cast<int *>(sx + NC * kTileM);              // [2][32] plane offsets (-1 = zero)
+  float *sgbuf = reinterpret_cast<float *>(jtab + 2 * 2 * kJB);       // [2][128]
   uint64_t *bars = reinterpret_cast<uint64_t *>((reinterpret_cast<uintptr_t>(sgbuf + 2 * kTileM) + 7) & ~(uintptr_t)7);
-  uint64_t *full = bars, *a_full = bars + 4, *s_empty = bars + 8;
-  uint64_t *jfull = bars + 12, *jempty = bars + 14, *gr_full = bars + 16, *gr_empty = bars + 18;
-  uint64_t *sg_full = bars + 20, *sg_empty = bars + 22, *final_bar = bars + 24;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 25);
+  uint64_t *a_full = bars, *s_empty = bars + 2, *jfull = bars + 4, *jempty = bars + 6;
+  uint64_t *gr_full = bars + 8, *gr_empty = bars + 10, *sg_full = bars + 12, *sg_empty = bars + 14;
+  uint64_t *final_bar = bars + 16;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 17);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
   DgPhases &ps = *reinterpret_cast<DgPhases *>(tmem_holder + 2);
   int2 *ptab = reinterpret_cast<int2 *>(&ps + 1);  // [T] tap table
@@ -270,8 +293,9 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   for (int e = threadIdx.x; e < p.T; e += blockDim.x) ptab[e] = dg_tap_entry(p, c, ps, e);
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&a_full[i], 128);
+      // 128 producer arrivals + the weight loader's arrival with the bytes of
+      // its copies
+      mbar_init(&a_full[i], 129);
       mbar_init(&s_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -324,36 +348,34 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           to[4 * q4 + 2] = t4.z;
           to[4 * q4 + 3] = t4.w;
         }
-        for (int ti = 0; ti < tg.ntaps; ++ti, ++it) {
+        for (int ti = 0; ti < tg.ntaps; ti += kTapsPS, ++it) {
           const uint32_t st = it % kStages, ph = (it / kStages) & 1;
-          if (!warp_wait(&full[st], ph, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // output pixel whose window puts this tap on the input pixel
-          const int dyx = ptab[tg.tap0 + ti].y;
-          const int oy = ay - (dyx >> 16), ox = bx - (dyx & 0xffff);
-          const bool valid = pvalid && oy >= 0 && ox >= 0 && oy < p.P && ox < p.Q;
-          const int ooff = (oy - tg.oylo) * p.Q + ox;
-          uint32_t hi[kKS], lo[kKS];
+          const uint32_t acol = tmem + lane_off + kColA + st * (kTapsPS * 64);
 #pragma unroll
-          for (int jl = 0; jl < kJB; ++jl) {
-            const int og = to[2 * jl], oh = to[2 * jl + 1];
-            const float gv = (valid && og >= 0) ? planes[og + ooff] : 0.f;
-            const float hv = (valid && oh >= 0) ? planes[oh + ooff] : 0.f;
-            sg += gv;
-            const float a0 = gv * hv, a1 = gv;
-            hi[2 * jl] = tf32_hi_bits(a0);
-            lo[2 * jl] = __float_as_uint(a0 - __uint_as_float(hi[2 * jl]));
-            hi[2 * jl + 1] = tf32_hi_bits(a1);
-            lo[2 * jl + 1] = __float_as_uint(a1 - __uint_as_float(hi[2 * jl + 1]));
+          for (int h = 0; h < kTapsPS; ++h) {
+            if (ti + h >= tg.ntaps) break;
+            // output pixel whose window puts this tap on the input pixel
+            const int dyx = ptab[tg.tap0 + ti + h].y;
+            const int oy = ay - (dyx >> 16), ox = bx - (dyx & 0xffff);
+            const bool valid = pvalid && oy >= 0 && ox >= 0 && oy < p.P && ox < p.Q;
+            uint32_t hi[kKS], lo[kKS];
+            dg_gather(planes, to, valid, (oy - tg.oylo) * p.Q + ox, sg, hi, lo);
+            if (h == 0) {
+              // the MMAs that read this A stage last have completed (the
+              // gather above needs only the staged planes, so it overlaps
+              // that wait)
+              if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            tmem_st16(acol + h * 64, *reinterpret_cast<const uint32_t(*)[16]>(&hi[0]));
+            tmem_st16(acol + h * 64 + 16, *reinterpret_cast<const uint32_t(*)[16]>(&hi[16]));
+            tmem_st16(acol + h * 64 + 32, *reinterpret_cast<const uint32_t(*)[16]>(&lo[0]));
+            tmem_st16(acol + h * 64 + 48, *reinterpret_cast<const uint32_t(*)[16]>(&lo[16]));
           }
-          const uint32_t acol = tmem + lane_off + kColA + st * 64;
-          tmem_st16(acol, *reinterpret_cast<const uint32_t(*)[16]>(&hi[0]));
-          tmem_st16(acol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&hi[16]));
-          tmem_st16(acol + 32, *reinterpret_cast<const uint32_t(*)[16]>(&lo[0]));
-          tmem_st16(acol + 48, *reinterpret_cast<const uint32_t(*)[16]>(&lo[16]));
+          if (!ok) break;
           tmem_st_wait();
           tc_fence_before();
           mbar_arrive(&a_full[st]);
@@ -380,7 +402,7 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       const int64_t t = item / c.ncb;
       const int cb = (int)(item - t * c.ncb);
       const DgGeo tg = dg_geo(p, c, ps, t);
-      const int ngroups = (c.nJB * tg.ntaps + kGroupStages - 1) / kGroupStages;
+      const int ngroups = c.nJB * ((tg.ntaps + kTapsPS - 1) / kTapsPS);
       // this pixel's input values are needed at the end of the item: copy
       // them to shared memory now, behind the item's MMAs (each thread reads
       // back only what it copied, so the cp.async wait alone orders them)
@@ -441,59 +463,106 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     cp_async_wait<0>();  // copies of an item left on an error path
   } else if (warp == 8) {
     // ------------------------------------------------------------- MMA
+    // One partial sum per stage (64 K): the stage's main MMAs back to back,
+    // then its corrections.
+    constexpr uint32_t kBTap = 2 * NC * 128;  // bytes of one tap's [W hi; W lo] tile
     const uint32_t id_main = idesc_tf32(kTileM, 2 * NC);
     const uint32_t id_corr = idesc_tf32(kTileM, NC);
     const uint32_t sB_addr = smem_u32(sB);
-    uint32_t it = 0, grp = 0;
+    uint32_t it = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
       const DgGeo tg = dg_geo(p, c, ps, item / c.ncb);
-      const int nk = c.nJB * tg.ntaps;
-      uint32_t dcol = 0, slot = 0;
-      for (int kq = 0; kq < nk; ++kq, ++it) {
-        const bool gstart = (kq % kGroupStages) == 0;
-        const bool gend = (kq % kGroupStages) == kGroupStages - 1 || kq == nk - 1;
-        if (gstart) {
-          slot = grp % kSlots;
-          if (!warp_wait(&gr_empty[slot], ((grp / kSlots) & 1) ^ 1, abort_flag)) {
+      for (int jb = 0; jb < c.nJB && ok; ++jb) {
+        for (int ti = 0; ti < tg.ntaps; ti += kTapsPS, ++it) {
+          const int nh = min(kTapsPS, tg.ntaps - ti);
+          const uint32_t slot = it % kSlots, st = it % kStages, ph = (it / kStages) & 1;
+          if (!warp_wait(&gr_empty[slot], ((it / kSlots) & 1) ^ 1, abort_flag) ||
+              !warp_wait(&a_full[st], ph, abort_flag)) {
             ok = false;
             break;
           }
-          dcol = tmem + slot * 128;
-        }
-        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
-        if (!warp_wait(&a_full[st], ph, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
+          tc_fence_after();
+          // straight-line issue from one elected lane (no branch between the
+          // MMAs of a stage)
+          const uint32_t dcol = tmem + slot * 128;
+          const uint32_t acol = tmem + kColA + st * (kTapsPS * 64);
+          const uint32_t bst = sB_addr + st * (kTapsPS * kBTap);  // per tap: rows W hi then W lo
+          if (elect_one()) {
+            if (nh == 2) {
 #pragma unroll
-          for (int ks = 0; ks < kKS / 8; ++ks) {
-            const uint32_t bhi = sB_addr + st * c.bstage + ks * 32;  // rows: W hi then W lo
-            const uint32_t acc = (gstart && ks == 0) ? 0u : 1u;
-            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(bhi), id_main, acc);
-            mma_tf32_ts(dcol + NC, alo + ks * 8, sdesc_kmajor_sw128(bhi), id_corr, 1u);
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int ks = 0; ks < kKS / 8; ++ks)
+                  mma_tf32_ts(dcol, acol + h * 64 + ks * 8, sdesc_kmajor_sw128(bst + h * kBTap + ks * 32), id_main,
+                              (h == 0 && ks == 0) ? 0u : 1u);
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int ks = 0; ks < kKS / 8; ++ks)
+                  mma_tf32_ts(dcol + NC, acol + h * 64 + 32 + ks * 8, sdesc_kmajor_sw128(bst + h * kBTap + ks * 32),
+                              id_corr, 1u);
+            } else {
+#pragma unroll
+              for (int ks = 0; ks < kKS / 8; ++ks)
+                mma_tf32_ts(dcol, acol + ks * 8, sdesc_kmajor_sw128(bst + ks * 32), id_main, ks == 0 ? 0u : 1u);
+#pragma unroll
+              for (int ks = 0; ks < kKS / 8; ++ks)
+                mma_tf32_ts(dcol + NC, acol + 32 + ks * 8, sdesc_kmajor_sw128(bst + ks * 32), id_corr, 1u);
+            }
+            tc_commit(&s_empty[st]);
+            tc_commit(&gr_full[slot]);
           }
-          tc_commit(&s_empty[st]);
-          if (gend) tc_commit(&gr_full[slot]);
+          __syncwarp();
         }
-        __syncwarp();
-        if (gend) ++grp;
       }
     }
-    if (lane == 0) tc_commit(final_bar);
+    if (elect_one()) tc_commit(final_bar);
     __syncwarp();
     mbar_wait(final_bar, 0, kWaitNs, nullptr);
-  } else {
-    // ------------------------------------------------------------- loader
-    uint32_t it = 0, jit = 0, jissued = 0;
+  } else if (warp == 9) {
+    // ---------------------------------------------------- weight loader
+    uint32_t it = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
       const int64_t t = item / c.ncb;
       const int cb = (int)(item - t * c.ncb);
       const DgGeo tg = dg_geo(p, c, ps, t);
+      for (int jb = 0; jb < c.nJB && ok; ++jb) {
+        for (int ti = 0; ti < tg.ntaps; ti += kTapsPS, ++it) {
+          const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+          if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            const int nh = min(kTapsPS, tg.ntaps - ti);
+            mbar_arrive_expect_tx(&a_full[st], (uint32_t)nh * c.bstage);
+            for (int h = 0; h < nh; ++h) {
+              const int tap = ptab[tg.tap0 + ti + h].x;
+              bulk_g2s(sB + ((size_t)st * kTapsPS + h) * c.bstage,
+                       wsB + ((int64_t)cb * c.nK + jb * p.T + tap) * 2 * c.NC * 32, c.bstage, &a_full[st]);
+            }
+          }
+          __syncwarp();
+        }
+      }
+    }
+    // Drain: the copies issued last have landed before the CTA exits (the
+    // phase also needs the producers' arrivals, which come on every path
+    // that issued the copies without an abort).
+    const uint32_t last = it < (uint32_t)kStages ? it : (uint32_t)kStages;
+    for (uint32_t i = 0; i < last; ++i) {
+      const uint32_t idx = it - 1 - i;
+      mbar_wait(&a_full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
+    }
+  } else {
+    // ------------------------------------------- g / hsum plane loader
+    // Runs up to two j-blocks ahead of the producers, independently of the
+    // weight stages.
+    uint32_t jit = 0;
+    for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
+      const DgGeo tg = dg_geo(p, c, ps, item / c.ncb);
       const int64_t run = (int64_t)tg.orows * p.Q;
-      for (int jb = 0; jb < c.nJB && ok; ++jb, ++jit) {
+      for (int jb = 0; jb < c.nJB; ++jb, ++jit) {
         const uint32_t js = jit & 1, jph = (jit >> 1) & 1;
         if (!warp_wait(&jempty[js], jph ^ 1, abort_flag)) {
           ok = false;
@@ -517,32 +586,11 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         __syncwarp();
         if (have) bulk_g2s(sJ + (size_t)js * c.jslot + (size_t)lane * c.PSo * 4, sp.src, sp.bytes, &jfull[js]);
         __syncwarp();
-        ++jissued;
-        for (int ti = 0; ti < tg.ntaps; ++ti, ++it) {
-          const uint32_t st = it % kStages, ph = (it / kStages) & 1;
-          if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          if (lane == 0) {
-            const int tap = ptab[tg.tap0 + ti].x;
-            mbar_arrive_expect_tx(&full[st], c.bstage);
-            bulk_g2s(sB + (size_t)st * c.bstage, wsB + ((int64_t)cb * c.nK + jb * p.T + tap) * 2 * c.NC * 32,
-                     c.bstage, &full[st]);
-          }
-          __syncwarp();
-        }
       }
     }
-    // Drain: the copies issued last have landed before the CTA exits.
-    const uint32_t last = it < (uint32_t)kStages ? it : (uint32_t)kStages;
-    for (uint32_t i = 0; i < last; ++i) {
-      const uint32_t idx = it - 1 - i;
-      mbar_wait(&full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
-    }
-    const uint32_t jlast = jissued < 2u ? jissued : 2u;
+    const uint32_t jlast = jit < 2u ? jit : 2u;
     for (uint32_t i = 0; i < jlast; ++i) {
-      const uint32_t idx = jissued - 1 - i;
+      const uint32_t idx = jit - 1 - i;
       mbar_wait(&jfull[idx & 1], (idx >> 1) & 1, kWaitNs, nullptr);
     }
   }
