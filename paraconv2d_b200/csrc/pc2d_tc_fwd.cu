@@ -393,6 +393,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   } else if (warp == 8) {
     // ------------------------------------------------------------- MMA
     const uint32_t idesc = idesc_tf32(kTileM, 2 * NB);
+    constexpr uint32_t kBlo = 2 * NB * 128;  // bytes of the hi rows of a B stage
     const uint32_t stage_addr = smem_u32(S.stage);
     uint32_t it = 0, grp = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
@@ -414,14 +415,16 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           break;
         }
         tc_fence_after();
-        if (lane == 0) {
-          const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
+        // straight-line issue from one elected lane, operands formed outside
+        const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
+        const uint32_t bhi0 = stage_addr + st * c.sstage;  // [H;P] rows, hi
+        const uint32_t acc0 = gstart ? 0u : 1u;
+        if (elect_one()) {
 #pragma unroll
           for (int ks = 0; ks < kKS / 8; ++ks) {
-            const uint32_t bhi = stage_addr + st * c.sstage + ks * 32;  // [H;P] rows, hi
-            const uint32_t blo = bhi + c.N * 128;                       // lo
-            const uint32_t acc = (gstart && ks == 0) ? 0u : 1u;
-            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(bhi), idesc, acc);
+            const uint32_t bhi = bhi0 + ks * 32;
+            const uint32_t blo = bhi + kBlo;  // lo
+            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(bhi), idesc, ks == 0 ? acc0 : 1u);
             mma_tf32_ts(dcol, alo + ks * 8, sdesc_kmajor_sw128(bhi), idesc, 1u);
             mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(blo), idesc, 1u);
           }
@@ -433,7 +436,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
       }
     }
     // Drain: every MMA issued by this warp completes before TMEM is freed.
-    if (lane == 0) tc_commit(S.final_bar);
+    if (elect_one()) tc_commit(S.final_bar);
     __syncwarp();
     mbar_wait(S.final_bar, 0, kWaitNs, nullptr);
   } else {

@@ -448,14 +448,16 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           break;
         }
         tc_fence_after();
-        if (lane == 0) {
-          const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
+        // straight-line issue from one elected lane, operands formed outside
+        const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
+        const uint32_t bhi0 = sB_addr + st * c.bstage, blo_off = c.NR * 128;
+        const uint32_t acc0 = gc == g0 ? 0u : 1u;
+        if (elect_one()) {
 #pragma unroll
           for (int ks = 0; ks < kChunk / 8; ++ks) {
-            const uint32_t bhi = sB_addr + st * c.bstage + ks * 32;
-            const uint32_t blo = bhi + c.NR * 128;
-            const uint32_t acc = (gc == g0 && ks == 0) ? 0u : 1u;
-            mma_tf32_ts(tmem, ahi + ks * 8, sdesc_kmajor_sw128(bhi), idesc, acc);
+            const uint32_t bhi = bhi0 + ks * 32;
+            const uint32_t blo = bhi + blo_off;
+            mma_tf32_ts(tmem, ahi + ks * 8, sdesc_kmajor_sw128(bhi), idesc, ks == 0 ? acc0 : 1u);
             mma_tf32_ts(tmem, alo + ks * 8, sdesc_kmajor_sw128(bhi), idesc, 1u);
             mma_tf32_ts(tmem, ahi + ks * 8, sdesc_kmajor_sw128(blo), idesc, 1u);
           }
@@ -465,10 +467,10 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         __syncwarp();
       }
       if (!ok) break;
-      if (lane == 0) tc_commit(d_full);
+      if (elect_one()) tc_commit(d_full);
       __syncwarp();
     }
-    if (lane == 0) tc_commit(final_bar);
+    if (elect_one()) tc_commit(final_bar);
     __syncwarp();
     mbar_wait(final_bar, 0, kWaitNs, nullptr);
   }
