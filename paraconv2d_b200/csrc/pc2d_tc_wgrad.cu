@@ -294,34 +294,42 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           break;
         }
         uint8_t *stg = sB + (size_t)st * c.bstage;
-        const float *halo = reinterpret_cast<const float *>(sH + (size_t)st * c.hstage);
-        const int *ro = roffs + st * 256;
-        const int poff = (oy * p.s0 - cg.ir0) * p.W + ox * p.s1;
-        const int64_t pbase = cg.n * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
-        for (int i0 = 0; i0 < nrows; i0 += 8) {
-          float v[8];
+        // row kl = bw + 8*i of the tile: v[i] = window element kl of this
+        // lane's pixel (0 past the chunk or the window range)
+        float v[32];
+        if (c.halo) {
+          // this warp's row offsets are contiguous in roffs[st][bw][i]: load
+          // them all first, then all the gathers, so the latencies overlap
+          const float *halo = reinterpret_cast<const float *>(sH + (size_t)st * c.hstage);
+          const int4 *ro4 = reinterpret_cast<const int4 *>(roffs + st * 256 + bw * 32);
+          const int poff = (oy * p.s0 - cg.ir0) * p.W + ox * p.s1;
+          int o[32];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int kl = bw + kBWarps * (i0 + u);
-            float a = 0.f;
-            if (c.halo) {
-              const int o = (i0 + u < nrows) ? ro[kl] : -1;
-              if (pvalid && o >= 0) a = halo[o + poff];
-            } else {
-              const int o = __shfl_sync(0xffffffffu, myoff, (i0 + u) & 31);
-              if (i0 + u < nrows && pvalid && o >= 0) a = __ldg(x + pbase + o);
-            }
-            v[u] = a;
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const int4 t = ro4[i4];
+            o[4 * i4] = t.x;
+            o[4 * i4 + 1] = t.y;
+            o[4 * i4 + 2] = t.z;
+            o[4 * i4 + 3] = t.w;
           }
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            if (i0 + u < nrows) {
-              const uint32_t kl = (uint32_t)(bw + kBWarps * (i0 + u));
-              const uint32_t hb = tf32_hi_bits(v[u]);
-              const uint32_t off = kl * 128 + ((((uint32_t)lane >> 2) ^ (kl & 7)) << 4) + cpos;
-              *reinterpret_cast<uint32_t *>(stg + off) = hb;
-              *reinterpret_cast<float *>(stg + (size_t)c.NR * 128 + off) = v[u] - __uint_as_float(hb);
-            }
+          for (int i = 0; i < 32; ++i) v[i] = (i < nrows && pvalid && o[i] >= 0) ? halo[o[i] + poff] : 0.f;
+        } else {
+          const int64_t pbase = cg.n * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int o = __shfl_sync(0xffffffffu, myoff, i);
+            v[i] = (i < nrows && pvalid && o >= 0) ? __ldg(x + pbase + o) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < nrows) {
+            const uint32_t kl = (uint32_t)(bw + kBWarps * i);
+            const uint32_t hb = tf32_hi_bits(v[i]);
+            const uint32_t off = kl * 128 + ((((uint32_t)lane >> 2) ^ (kl & 7)) << 4) + cpos;
+            *reinterpret_cast<uint32_t *>(stg + off) = hb;
+            *reinterpret_cast<float *>(stg + (size_t)c.NR * 128 + off) = v[i] - __uint_as_float(hb);
           }
         }
         fence_proxy_async_smem();
@@ -407,9 +415,11 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           __syncwarp();
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
+            // row kl goes to B-producer warp kl % 8, slot kl / 8 (entries past
+            // NR stay -1, read as zero rows)
             const int kl = lane + 32 * e;
-            if (kl < c.NR)
-              roffs[st * 256 + kl] = rc[e] >= 0 ? rc[e] * c.PSw + lead[st * 64 + rc[e]] + rt[e] : -1;
+            roffs[st * 256 + (kl % kBWarps) * 32 + kl / kBWarps] =
+                (kl < c.NR && rc[e] >= 0) ? rc[e] * c.PSw + lead[st * 64 + rc[e]] + rt[e] : -1;
           }
           __syncwarp();
           if (lane == 0) mbar_arrive_expect_tx(&h_full[st], bytes);
