@@ -94,6 +94,23 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// Shared-memory accesses by 32-bit shared-window address (ld/st.shared, never
+// a generic access).  Volatile: they keep their order relative to the
+// barrier waits around them.
+__device__ __forceinline__ float lds_f32(uint32_t saddr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(saddr));
+  return v;
+}
+__device__ __forceinline__ int4 lds_v4s32(uint32_t saddr) {
+  int4 v;
+  asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(saddr));
+  return v;
+}
+__device__ __forceinline__ void sts_u32(uint32_t saddr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(saddr), "r"(v));
+}
+
 // Hint: bring the line holding `p` into L2 (no register result, no wait).
 __device__ __forceinline__ void prefetch_l2(const void *p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));

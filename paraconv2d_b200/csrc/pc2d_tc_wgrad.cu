@@ -293,27 +293,28 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           ok = false;
           break;
         }
-        uint8_t *stg = sB + (size_t)st * c.bstage;
+        const uint32_t stg_a = smem_u32(sB + (size_t)st * c.bstage), lo_off = (uint32_t)c.NR * 128;
         // row kl = bw + 8*i of the tile: v[i] = window element kl of this
         // lane's pixel (0 past the chunk or the window range)
         float v[32];
         if (c.halo) {
           // this warp's row offsets are contiguous in roffs[st][bw][i]: load
           // them all first, then all the gathers, so the latencies overlap
-          const float *halo = reinterpret_cast<const float *>(sH + (size_t)st * c.hstage);
-          const int4 *ro4 = reinterpret_cast<const int4 *>(roffs + st * 256 + bw * 32);
+          const uint32_t halo = smem_u32(sH + (size_t)st * c.hstage);
+          const uint32_t ro4 = smem_u32(roffs + st * 256 + bw * 32);
           const int poff = (oy * p.s0 - cg.ir0) * p.W + ox * p.s1;
           int o[32];
 #pragma unroll
           for (int i4 = 0; i4 < 8; ++i4) {
-            const int4 t = ro4[i4];
+            const int4 t = lds_v4s32(ro4 + 16 * i4);
             o[4 * i4] = t.x;
             o[4 * i4 + 1] = t.y;
             o[4 * i4 + 2] = t.z;
             o[4 * i4 + 3] = t.w;
           }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = (i < nrows && pvalid && o[i] >= 0) ? halo[o[i] + poff] : 0.f;
+          for (int i = 0; i < 32; ++i)
+            v[i] = (i < nrows && pvalid && o[i] >= 0) ? lds_f32(halo + 4u * (uint32_t)(o[i] + poff)) : 0.f;
         } else {
           const int64_t pbase = cg.n * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
 #pragma unroll
@@ -328,8 +329,8 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
             const uint32_t kl = (uint32_t)(bw + kBWarps * i);
             const uint32_t hb = tf32_hi_bits(v[i]);
             const uint32_t off = kl * 128 + ((((uint32_t)lane >> 2) ^ (kl & 7)) << 4) + cpos;
-            *reinterpret_cast<uint32_t *>(stg + off) = hb;
-            *reinterpret_cast<float *>(stg + (size_t)c.NR * 128 + off) = v[i] - __uint_as_float(hb);
+            sts_u32(stg_a + off, hb);
+            sts_u32(stg_a + lo_off + off, __float_as_uint(v[i] - __uint_as_float(hb)));
           }
         }
         fence_proxy_async_smem();
