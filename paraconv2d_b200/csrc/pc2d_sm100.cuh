@@ -116,6 +116,18 @@ __device__ __forceinline__ void prefetch_l2(const void *p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+// 2-D tensor copy (TMA, tiled, no multicast) of the box at element (x, y) of
+// the tensor map `tmap` (the address of a __grid_constant__ CUtensorMap) into
+// this CTA's shared memory, completing on `bar` with the full box bytes.  x
+// times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 4-byte asynchronous copy global -> shared (LDGSTS).  With valid == false no
 // global byte is read and the destination is zero-filled.
 __device__ __forceinline__ void cp_async4(void *smem_dst, const void *gmem_src, bool valid) {

@@ -34,7 +34,10 @@
 // producers, 12-15 epilogue, 16 MMA issuer and TMEM owner, 17 loader of the
 // input rows the B producers gather from.  All waits are bounded as in the
 // forward kernel.
+#include <cuda.h>  // CUtensorMap (types only; the encoder is resolved at run time)
+
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "pc2d_tc.cuh"
@@ -69,6 +72,7 @@ struct WgCfg {
   int nchm;         // channels a window-row range touches at most
   int PSw;          // staged plane stride (floats, multiple of 4)
   uint32_t hstage;  // halo bytes per stage (multiple of 1024)
+  int tma;          // 1: the halo of a chunk is one 2-D tensor copy [nchm][PSw] (see tc_wgrad)
 };
 
 WgCfg wg_cfg(const Problem &p, int sms) {
@@ -95,9 +99,16 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   c.PSw = (int)(((int64_t)rows * p.W + 8 + 3) / 4 * 4);
   c.hstage = (uint32_t)align_up((size_t)c.nchm * c.PSw * 4, 1024);
   c.halo = c.nchm <= 64 ? 1 : 0;
+  // One 2-D tensor copy per chunk needs the channel plane stride to be a
+  // multiple of 16 bytes; its box is the staged plane (PSw floats from the
+  // 16-byte boundary at or below the chunk's first element), at most 256.
+  c.tma = (p.HW % 4 == 0 && c.PSw <= 256 && (int64_t)p.n * p.C < ((int64_t)1 << 31)) ? 1 : 0;
   const size_t need = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256) * 4 + 16 * 8 + 64;
   if (need > (size_t)kSmemLimit) c.halo = 0;  // gather from global memory instead
-  if (!c.halo) c.hstage = 0;
+  if (!c.halo) {
+    c.hstage = 0;
+    c.tma = 0;
+  }
   return c;
 }
 
@@ -132,7 +143,8 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 __global__ void __launch_bounds__(kThreads, 1)
 tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, const float *__restrict__ hsum,
-                Problem p, WgCfg c, float *__restrict__ part, float *__restrict__ sums, int *status) {
+                Problem p, WgCfg c, const __grid_constant__ CUtensorMap xmap, float *__restrict__ part,
+                float *__restrict__ sums, int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -403,6 +415,26 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
             break;
           }
           const ChunkGeo cg = chunk_geo(p, c, gc);
+          uint8_t *hb = sH + (size_t)st * c.hstage;
+          if (c.tma) {
+            // one tensor copy: channels clo .. clo+nchm-1 of image n, each
+            // from the 16-byte boundary at or below the chunk's first input
+            // element (zero past the end of the tensor)
+            const int xo = cg.ir0 * p.W, x0 = xo & ~3, ld = xo - x0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int kl = lane + 32 * e;
+              roffs[st * 256 + (kl % kBWarps) * 32 + kl / kBWarps] =
+                  (kl < c.NR && rc[e] >= 0) ? rc[e] * c.PSw + ld + rt[e] : -1;
+            }
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&h_full[st], (uint32_t)(c.nchm * c.PSw * 4));
+              tma_load_2d(hb, &xmap, x0, (int)(cg.n * p.C + clo), &h_full[st]);
+            }
+            __syncwarp();
+            continue;
+          }
           const float *xrow = x + cg.n * p.CHW + (int64_t)cg.ir0 * p.W;
           const int64_t run = (int64_t)cg.rows * p.W;
           uint32_t bytes = 0;
@@ -425,7 +457,6 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           __syncwarp();
           if (lane == 0) mbar_arrive_expect_tx(&h_full[st], bytes);
           __syncwarp();
-          uint8_t *hb = sH + (size_t)st * c.hstage;
           for (int ci = lane; ci < nch; ci += 32) {
             const tc::BulkSpan sp = tc::bulk_span(xrow + (int64_t)(clo + ci) * p.HW, run);
             bulk_g2s(hb + (size_t)ci * c.PSw * 4, sp.src, sp.bytes, &h_full[st]);
@@ -556,6 +587,38 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
 std::mutex g_attr_mutex;
 bool g_attr_set[64] = {};
 
+// cuTensorMapEncodeTiled, resolved once through the runtime (no link-time
+// dependency on the driver library).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// x viewed as a 2-D tensor [n*C rows][HW floats], boxes of nchm rows x PSw
+// floats, zero fill outside.
+bool encode_x_map(const Problem &p, const WgCfg &c, const float *x, CUtensorMap *map) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)p.HW, (cuuint64_t)p.n * p.C};
+  const cuuint64_t strides[1] = {(cuuint64_t)p.HW * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)c.PSw, (cuuint32_t)c.nchm};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool tc_wgrad_supported(const Problem &p) {
@@ -571,7 +634,10 @@ size_t tc_wgrad_workspace(const Problem &p) {
 
 int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, double factor,
              float *dpars, void *ws, cudaStream_t stream) {
-  const WgCfg c = wg_cfg(p, device_sm_count());
+  WgCfg c = wg_cfg(p, device_sm_count());
+  CUtensorMap xmap;
+  std::memset(&xmap, 0, sizeof(xmap));
+  if (c.tma && !encode_x_map(p, c, x, &xmap)) c.tma = 0;  // per-channel bulk copies instead (same layout)
   int *status = device_status_ptr();
   if (!status) {
     set_last_error("could not resolve the device status word");
@@ -590,7 +656,7 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   }
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
   timing_begin(K_WGRAD, stream);
-  tc_wgrad_kernel<<<grid, kThreads, wg_smem_bytes(c), stream>>>(grad, x, hsum, p, c, part, sums, status);
+  tc_wgrad_kernel<<<grid, kThreads, wg_smem_bytes(c), stream>>>(grad, x, hsum, p, c, xmap, part, sums, status);
   timing_end(K_WGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
   const dim3 fgrid(ceil_div(p.d, 256), p.m);
