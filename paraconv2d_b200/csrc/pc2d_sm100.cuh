@@ -110,6 +110,9 @@ __device__ __forceinline__ int4 lds_v4s32(uint32_t saddr) {
 __device__ __forceinline__ void sts_u32(uint32_t saddr, uint32_t v) {
   asm volatile("st.shared.u32 [%0], %1;" ::"r"(saddr), "r"(v));
 }
+__device__ __forceinline__ void sts_v4u32(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d));
+}
 
 // Hint: bring the line holding `p` into L2 (no register result, no wait).
 __device__ __forceinline__ void prefetch_l2(const void *p) {

@@ -269,11 +269,10 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     }
   } else if (warp < 4 + kBWarps) {
     // -------------------------------------------------------- B producers
-    // Warp bw builds rows kl = bw + 8*i of each chunk's B tile (lane = pixel).
-    // With c.halo the window values come from the input rows the loader warp
-    // staged in shared memory (per-row offsets in roffs[stage]); otherwise
-    // they are gathered from global memory (lane i holds the input offset of
-    // row bw + 8*i of the item's window range).
+    // Warp bw builds rows kl = bw + 8*i of each chunk's B tile.  With c.halo
+    // the window values come from the input rows the loader warp staged in
+    // shared memory (this warp's row offsets in roffs[stage][bw][i]);
+    // otherwise they are gathered from global memory.
     const int bw = warp - 4;
     const int nrows = (c.NR - bw + kBWarps - 1) / kBWarps;  // <= 32
     const uint32_t cpos = (uint32_t)(lane & 3) * 4;
@@ -306,43 +305,68 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           break;
         }
         const uint32_t stg_a = smem_u32(sB + (size_t)st * c.bstage), lo_off = (uint32_t)c.NR * 128;
-        // row kl = bw + 8*i of the tile: v[i] = window element kl of this
-        // lane's pixel (0 past the chunk or the window range)
-        float v[32];
         if (c.halo) {
-          // this warp's row offsets are contiguous in roffs[st][bw][i]: load
-          // them all first, then all the gathers, so the latencies overlap
+          // Lane = (row slot rr = lane / 8, 4-pixel group g = lane % 8): it
+          // writes the 16-byte chunk g of rows kl = bw + 8*(4*i + rr) (hi and
+          // lo), i.e. pixels 4g .. 4g+3 of the chunk, gathered from the input
+          // rows the loader staged.  kl % 8 == bw, so the swizzled position
+          // of chunk g is g ^ bw for every row of this warp.
+          const int g = lane & 7, rr = lane >> 3;
           const uint32_t halo = smem_u32(sH + (size_t)st * c.hstage);
-          const uint32_t ro4 = smem_u32(roffs + st * 256 + bw * 32);
-          const int poff = (oy * p.s0 - cg.ir0) * p.W + ox * p.s1;
-          int o[32];
+          const int *ro = roffs + st * 256 + bw * 32;
+          int poff[4];
+          bool pv[4];
 #pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4) {
-            const int4 t = lds_v4s32(ro4 + 16 * i4);
-            o[4 * i4] = t.x;
-            o[4 * i4 + 1] = t.y;
-            o[4 * i4 + 2] = t.z;
-            o[4 * i4 + 3] = t.w;
+          for (int j = 0; j < 4; ++j) {
+            const int px = 4 * g + j, q = cg.pq0 + px;
+            const int qy = q / p.Q, qx = q - qy * p.Q;
+            pv[j] = px < cg.npx;
+            poff[j] = (qy * p.s0 - cg.ir0) * p.W + qx * p.s1;
           }
+          const uint32_t cbyte = (uint32_t)((g ^ bw) << 4);
+          int o[8];
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            v[i] = (i < nrows && pvalid && o[i] >= 0) ? lds_f32(halo + 4u * (uint32_t)(o[i] + poff)) : 0.f;
+          for (int i = 0; i < 8; ++i) o[i] = (4 * i + rr < nrows) ? ro[4 * i + rr] : -1;
+          float v[8][4];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              v[i][j] = (pv[j] && o[i] >= 0) ? lds_f32(halo + 4u * (uint32_t)(o[i] + poff[j])) : 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (4 * i + rr < nrows) {
+              const uint32_t kl = (uint32_t)(bw + kBWarps * (4 * i + rr));
+              uint32_t h[4], l[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                h[j] = tf32_hi_bits(v[i][j]);
+                l[j] = __float_as_uint(v[i][j] - __uint_as_float(h[j]));
+              }
+              const uint32_t a = stg_a + kl * 128 + cbyte;
+              sts_v4u32(a, h[0], h[1], h[2], h[3]);
+              sts_v4u32(a + lo_off, l[0], l[1], l[2], l[3]);
+            }
+          }
         } else {
+          // lane = pixel; row kl = bw + 8*i gathered from global memory (lane
+          // i holds the input offset of row bw + 8*i of the window range)
           const int64_t pbase = cg.n * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
+          float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int o = __shfl_sync(0xffffffffu, myoff, i);
             v[i] = (i < nrows && pvalid && o >= 0) ? __ldg(x + pbase + o) : 0.f;
           }
-        }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < nrows) {
-            const uint32_t kl = (uint32_t)(bw + kBWarps * i);
-            const uint32_t hb = tf32_hi_bits(v[i]);
-            const uint32_t off = kl * 128 + ((((uint32_t)lane >> 2) ^ (kl & 7)) << 4) + cpos;
-            sts_u32(stg_a + off, hb);
-            sts_u32(stg_a + lo_off + off, __float_as_uint(v[i] - __uint_as_float(hb)));
+          for (int i = 0; i < 32; ++i) {
+            if (i < nrows) {
+              const uint32_t kl = (uint32_t)(bw + kBWarps * i);
+              const uint32_t hb = tf32_hi_bits(v[i]);
+              const uint32_t off = kl * 128 + ((((uint32_t)lane >> 2) ^ (kl & 7)) << 4) + cpos;
+              sts_u32(stg_a + off, hb);
+              sts_u32(stg_a + lo_off + off, __float_as_uint(v[i] - __uint_as_float(hb)));
+            }
           }
         }
         fence_proxy_async_smem();
