@@ -555,13 +555,19 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
 
 // Fixed-order fp64 reduction of the per-segment partials and the parameter
 // gradient epilogue:  dh = 2f dH, dp = 2f (dP - p SG), dh0 = 2f S1,
-// dp0 = -2f p0 SG.  Grid (ceil(d/256), m).
+// dp0 = -2f p0 SG.  Grid (ceil(d/64), m), 256 threads: thread (q, kx) sums
+// the segments s = q, q+4, ... of window element 64*blockIdx.x + kx, and the
+// four partials are added in the order q = 0..3, so the result does not
+// depend on timing.
+constexpr int kFinK = 64;
 __global__ void __launch_bounds__(256)
 tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums, const float *__restrict__ pars,
                   Problem p, WgCfg c, double f2, float *__restrict__ dpars) {
   __shared__ double s_sums[2];
+  __shared__ double s_part[2][4][kFinK];
   const int j = blockIdx.y;
-  const int64_t k = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  const int kx = threadIdx.x % kFinK, q = threadIdx.x / kFinK;
+  const int64_t k = (int64_t)blockIdx.x * kFinK + kx;
   const int mb = j / c.JM, jl = j - mb * c.JM;
   const int r1 = jl, r2 = c.JM + jl;
   const int per = c.nNR * c.nmb;
@@ -582,25 +588,31 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
       s_sums[1] = b;
     }
   }
-  __syncthreads();
-  const double s1 = s_sums[0], sg = s_sums[1];
-  const int m = p.m;
   const int64_t d = p.d;
-  const float *pp = pars + m + (int64_t)m * d;
-  const float *p0 = pp + (int64_t)m * d;
-  float *dh0 = dpars, *dh = dpars + m, *dpp = dh + (int64_t)m * d, *dp0 = dpp + (int64_t)m * d;
+  double ah = 0.0, ap = 0.0;
   if (k < d) {
     const int nr = (int)(k / c.NR);
     const int kl = (int)(k - (int64_t)nr * c.NR);
-    double ah = 0.0, ap = 0.0;
-    for (int64_t s = 0; s < c.nseg; ++s) {
+    for (int64_t s = q; s < c.nseg; s += 4) {
       const int64_t item = (s * c.nNR + nr) * c.nmb + mb;
       ah += (double)part[(item * 128 + r1) * c.NR + kl];
       ap += (double)part[(item * 128 + r2) * c.NR + kl];
     }
+  }
+  s_part[0][q][kx] = ah;
+  s_part[1][q][kx] = ap;
+  __syncthreads();
+  const double s1 = s_sums[0], sg = s_sums[1];
+  const int m = p.m;
+  const float *pp = pars + m + (int64_t)m * d;
+  const float *p0 = pp + (int64_t)m * d;
+  float *dh0 = dpars, *dh = dpars + m, *dpp = dh + (int64_t)m * d, *dp0 = dpp + (int64_t)m * d;
+  if (q == 0 && k < d) {
+    const double th = ((s_part[0][0][kx] + s_part[0][1][kx]) + s_part[0][2][kx]) + s_part[0][3][kx];
+    const double tp = ((s_part[1][0][kx] + s_part[1][1][kx]) + s_part[1][2][kx]) + s_part[1][3][kx];
     const int64_t wi = (int64_t)j * d + k;
-    dh[wi] = (float)(f2 * ah);
-    dpp[wi] = (float)(f2 * (ap - (double)pp[wi] * sg));
+    dh[wi] = (float)(f2 * th);
+    dpp[wi] = (float)(f2 * (tp - (double)pp[wi] * sg));
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     dh0[j] = (float)(f2 * s1);
@@ -683,7 +695,7 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   tc_wgrad_kernel<<<grid, kThreads, wg_smem_bytes(c), stream>>>(grad, x, hsum, p, c, xmap, part, sums, status);
   timing_end(K_WGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
-  const dim3 fgrid(ceil_div(p.d, 256), p.m);
+  const dim3 fgrid(ceil_div(p.d, kFinK), p.m);
   tc_wgrad_finalize<<<fgrid, 256, 0, stream>>>(part, sums, pars, p, c, 2.0 * (double)(float)factor, dpars);
   PC2D_LAUNCH_CHECK("tc_wgrad_finalize");
   return PC2D_OK;
