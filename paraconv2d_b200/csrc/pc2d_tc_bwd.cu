@@ -21,8 +21,9 @@
 //     the 16 channels of the stage from the staged planes, accumulate SG,
 //     split into tf32 hi + lo and tcgen05.st them into TMEM (A operand).  A
 //     producer reuses an A slot as soon as the MMAs that read it complete;
-//   - warps 4-7, epilogue: drain the partial sums (a fresh one every 64 K, in
-//     one of two TMEM slots) into fp32 registers, and write
+//   - warps 4-7, epilogue: drain the partial sums (a fresh one per j-block of
+//     16 output channels, in one of two TMEM slots) into fp32 registers, and
+//     write
 //     dx = 2 * (acc - x * SG), with x copied to shared memory (cp.async) at
 //     the start of the tile;
 //   - warp 8, MMA (one thread): per 8-wide K step two MMAs
@@ -55,7 +56,7 @@ constexpr int kKS = 32;
 constexpr int kJB = 16;          // output channels per j-block (32 K per tap)
 constexpr int kStages = 2;       // A/B stages of kTapsPS taps (64 K) each
 constexpr int kTapsPS = 2;       // taps per stage
-constexpr int kSlots = 2;        // accumulator slots (one partial sum per stage)
+constexpr int kSlots = 2;        // accumulator slots (one partial sum per j-block)
 constexpr int kMaxNC = 64;
 constexpr int kThreads = 352;
 constexpr int kMinSmem = 120 * 1024;
@@ -402,7 +403,7 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       const int64_t t = item / c.ncb;
       const int cb = (int)(item - t * c.ncb);
       const DgGeo tg = dg_geo(p, c, ps, t);
-      const int ngroups = c.nJB * ((tg.ntaps + kTapsPS - 1) / kTapsPS);
+      const int ngroups = tg.ntaps > 0 ? c.nJB : 0;  // one partial sum per j-block
       // this pixel's input values are needed at the end of the item: copy
       // them to shared memory now, behind the item's MMAs (each thread reads
       // back only what it copied, so the cp.async wait alone orders them)
@@ -463,30 +464,39 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     cp_async_wait<0>();  // copies of an item left on an error path
   } else if (warp == 8) {
     // ------------------------------------------------------------- MMA
-    // One partial sum per stage (64 K): the stage's main MMAs back to back,
-    // then its corrections.
+    // One partial sum per j-block (2 x 16 x taps K, e.g. 288 for a 3x3
+    // window): a fresh accumulator slot at the j-block's first stage,
+    // drained by the epilogue after its last.  Within a stage the main MMAs
+    // go back to back, then the corrections.
     constexpr uint32_t kBTap = 2 * NC * 128;  // bytes of one tap's [W hi; W lo] tile
     const uint32_t id_main = idesc_tf32(kTileM, 2 * NC);
     const uint32_t id_corr = idesc_tf32(kTileM, NC);
     const uint32_t sB_addr = smem_u32(sB);
-    uint32_t it = 0;
+    uint32_t it = 0, grp = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
       const DgGeo tg = dg_geo(p, c, ps, item / c.ncb);
-      for (int jb = 0; jb < c.nJB && ok; ++jb) {
+      if (tg.ntaps == 0) continue;
+      for (int jb = 0; jb < c.nJB && ok; ++jb, ++grp) {
+        const uint32_t slot = grp % kSlots;
+        if (!warp_wait(&gr_empty[slot], ((grp / kSlots) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t dcol = tmem + slot * 128;
         for (int ti = 0; ti < tg.ntaps; ti += kTapsPS, ++it) {
           const int nh = min(kTapsPS, tg.ntaps - ti);
-          const uint32_t slot = it % kSlots, st = it % kStages, ph = (it / kStages) & 1;
-          if (!warp_wait(&gr_empty[slot], ((it / kSlots) & 1) ^ 1, abort_flag) ||
-              !warp_wait(&a_full[st], ph, abort_flag)) {
+          const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+          if (!warp_wait(&a_full[st], ph, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           // straight-line issue from one elected lane (no branch between the
           // MMAs of a stage)
-          const uint32_t dcol = tmem + slot * 128;
           const uint32_t acol = tmem + kColA + st * (kTapsPS * 64);
           const uint32_t bst = sB_addr + st * (kTapsPS * kBTap);  // per tap: rows W hi then W lo
+          const uint32_t acc0 = ti == 0 ? 0u : 1u;
+          const bool last = ti + kTapsPS >= tg.ntaps;
           if (elect_one()) {
             if (nh == 2) {
 #pragma unroll
@@ -494,7 +504,7 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
 #pragma unroll
                 for (int ks = 0; ks < kKS / 8; ++ks)
                   mma_tf32_ts(dcol, acol + h * 64 + ks * 8, sdesc_kmajor_sw128(bst + h * kBTap + ks * 32), id_main,
-                              (h == 0 && ks == 0) ? 0u : 1u);
+                              (h == 0 && ks == 0) ? acc0 : 1u);
 #pragma unroll
               for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -504,13 +514,13 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
             } else {
 #pragma unroll
               for (int ks = 0; ks < kKS / 8; ++ks)
-                mma_tf32_ts(dcol, acol + ks * 8, sdesc_kmajor_sw128(bst + ks * 32), id_main, ks == 0 ? 0u : 1u);
+                mma_tf32_ts(dcol, acol + ks * 8, sdesc_kmajor_sw128(bst + ks * 32), id_main, ks == 0 ? acc0 : 1u);
 #pragma unroll
               for (int ks = 0; ks < kKS / 8; ++ks)
                 mma_tf32_ts(dcol + NC, acol + 32 + ks * 8, sdesc_kmajor_sw128(bst + ks * 32), id_corr, 1u);
             }
             tc_commit(&s_empty[st]);
-            tc_commit(&gr_full[slot]);
+            if (last) tc_commit(&gr_full[slot]);
           }
           __syncwarp();
         }
