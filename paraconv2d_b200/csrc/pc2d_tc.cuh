@@ -1,6 +1,8 @@
 // Host entry points of the tcgen05 (tensor-core, 3xTF32) kernels.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (types only; the encoder is resolved at run time)
+
 #include "pc2d_common.cuh"
 
 namespace pc2d {
@@ -29,5 +31,11 @@ int tc_selftest_bounded_wait(unsigned int timeout_us, int *status, cudaStream_t 
 
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
+
+// Tensor map of the input planes for one 2-D TMA copy per stage: x viewed as
+// rows = n*C channel planes of HW floats, boxes of box_rows planes x box_inner
+// floats, zero fill outside.  False (map unusable) when the driver entry point
+// is missing, x is not 16-byte aligned or HW*4 is not a multiple of 16.
+bool encode_planes_map(const float *x, int64_t HW, int64_t rows, int box_inner, int box_rows, CUtensorMap *map);
 
 }  // namespace pc2d

@@ -38,6 +38,7 @@
 //   records PC2D_ERR_TIMEOUT, raises a CTA-wide abort flag, and the CTA
 //   drains its in-flight copies and MMAs and exits.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "pc2d_tc.cuh"
@@ -76,6 +77,7 @@ struct FwdCfg {
   int nchs;         // channels a stage touches at most (<= 32)
   uint32_t bstage;  // B bytes per stage (hi + lo)
   uint32_t sstage;  // shared bytes per stage (B + halo, multiple of 1024)
+  int tma;          // 1: a stage's halo is one 2-D tensor copy [nchs planes][PS floats]
 };
 
 FwdCfg fwd_cfg(const Problem &p) {
@@ -103,6 +105,10 @@ FwdCfg fwd_cfg(const Problem &p) {
   const size_t hb = align_up((size_t)c.nchs * c.PS * 4, 1024);
   c.sstage = (uint32_t)(c.bstage + hb);
   c.nst = kMaxStages;
+  // one tensor copy per stage: channel planes 16-byte strided, the plane
+  // stride PS (from the 16-byte boundary at or below the tile's first input
+  // element) at most 256 floats
+  c.tma = (p.HW % 4 == 0 && c.PS <= 256 && (int64_t)p.n * p.C < ((int64_t)1 << 31)) ? 1 : 0;
   return c;
 }
 
@@ -203,8 +209,9 @@ struct Smem {
 template <int NB>
 __global__ void __launch_bounds__(kFwdThreads, 1)
 tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, const float *__restrict__ wsB,
-                  const float *__restrict__ cj, float factor, Problem p, FwdCfg c, float *__restrict__ out,
-                  float *__restrict__ hsum, int *status) {
+                  const float *__restrict__ cj, float factor, Problem p, FwdCfg c,
+                  const __grid_constant__ CUtensorMap xmap, float *__restrict__ out, float *__restrict__ hsum,
+                  int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -454,9 +461,26 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           ok = false;
           break;
         }
+        const int clo = S.koff[kq * kKS].x;
+        uint8_t *sbase = S.stage + (size_t)st * c.sstage;
+        if (c.tma) {
+          // one tensor copy: planes clo .. clo+nchs-1 of image n, PS floats
+          // each from the 16-byte boundary at or below the tile's first input
+          // element (zero past the end of the tensor)
+          const int xo = tg.ir0 * p.W, x0 = xo & ~3, ld = xo - x0;
+          const int2 ko = S.koff[kq * kKS + lane];
+          S.offs[st * kKS + lane] = ko.x >= 0 ? (ko.x - clo) * c.PS + ld + ko.y : -1;
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&S.full[st], c.bstage + (uint32_t)(c.nchs * c.PS * 4));
+            bulk_g2s(sbase, wsB + ((int64_t)cb * c.nK + kq) * 2 * c.N * 32, c.bstage, &S.full[st]);
+            tma_load_2d(sbase + c.bstage, &xmap, x0, (int)(tg.n * p.C + clo), &S.full[st]);
+          }
+          __syncwarp();
+          continue;
+        }
         // Channel planes of the stage (one lane each): 16-byte-rounded spans,
         // their leads and the total byte count.
-        const int clo = S.koff[kq * kKS].x;
         int chi = clo;
 #pragma unroll 1
         for (int kk = kKS - 1; kk >= 0; --kk) {
@@ -484,7 +508,6 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
               ko.x >= 0 ? (ko.x - clo) * c.PS + S.lead[st * 32 + (ko.x - clo)] + ko.y : -1;
         }
         __syncwarp();
-        uint8_t *sbase = S.stage + (size_t)st * c.sstage;
         if (lane == 0) {
           mbar_arrive_expect_tx(&S.full[st], c.bstage + bytes);
           bulk_g2s(sbase, wsB + ((int64_t)cb * c.nK + kq) * 2 * c.N * 32, c.bstage, &S.full[st]);
@@ -530,8 +553,12 @@ bool g_attr_set[64][4] = {};
 int g_sm_count[64] = {0};
 
 template <int NB>
-int launch_forward(const Problem &p, const FwdCfg &c, const float *x, const float *pars, const float *wsB,
+int launch_forward(const Problem &p, FwdCfg c, const float *x, const float *pars, const float *wsB,
                    const float *cj, float factor, float *out, float *hsum, int *status, cudaStream_t stream) {
+  CUtensorMap xmap;
+  std::memset(&xmap, 0, sizeof(xmap));
+  if (c.tma && !encode_planes_map(x, p.HW, (int64_t)p.n * p.C, c.PS, c.nchs, &xmap))
+    c.tma = 0;  // per-channel bulk copies instead (same layout)
   int dev = 0;
   PC2D_CUDA_CHECK(cudaGetDevice(&dev));
   {
@@ -544,14 +571,48 @@ int launch_forward(const Problem &p, const FwdCfg &c, const float *x, const floa
   }
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
   timing_begin(K_FORWARD, stream);
-  tc_forward_kernel<NB><<<grid, kFwdThreads, fwd_smem_bytes(p, c), stream>>>(x, pars, wsB, cj, factor, p, c, out, hsum,
-                                                                          status);
+  tc_forward_kernel<NB><<<grid, kFwdThreads, fwd_smem_bytes(p, c), stream>>>(x, pars, wsB, cj, factor, p, c, xmap, out,
+                                                                          hsum, status);
   timing_end(K_FORWARD, stream);
   PC2D_LAUNCH_CHECK("tc_forward_kernel");
   return PC2D_OK;
 }
 
 }  // namespace
+
+namespace {
+// cuTensorMapEncodeTiled, resolved once through the runtime (no link-time
+// dependency on the driver library).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+}  // namespace
+
+bool encode_planes_map(const float *x, int64_t HW, int64_t rows, int box_inner, int box_rows, CUtensorMap *map) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || (reinterpret_cast<uintptr_t>(x) & 15) != 0 || HW % 4 != 0 || box_inner % 4 != 0 || box_inner < 4 ||
+      box_inner > 256 || box_rows < 1 || box_rows > 256 || rows < 1)
+    return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)HW, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)HW * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 int device_sm_count() {
   int dev = 0;

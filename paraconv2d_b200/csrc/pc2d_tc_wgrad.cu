@@ -34,8 +34,6 @@
 // producers, 12-15 epilogue, 16 MMA issuer and TMEM owner, 17 loader of the
 // input rows the B producers gather from.  All waits are bounded as in the
 // forward kernel.
-#include <cuda.h>  // CUtensorMap (types only; the encoder is resolved at run time)
-
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -623,38 +621,6 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
 std::mutex g_attr_mutex;
 bool g_attr_set[64] = {};
 
-// cuTensorMapEncodeTiled, resolved once through the runtime (no link-time
-// dependency on the driver library).
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiledFn encode_tiled() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  });
-  return fn;
-}
-
-// x viewed as a 2-D tensor [n*C rows][HW floats], boxes of nchm rows x PSw
-// floats, zero fill outside.
-bool encode_x_map(const Problem &p, const WgCfg &c, const float *x, CUtensorMap *map) {
-  EncodeTiledFn fn = encode_tiled();
-  if (!fn || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)p.HW, (cuuint64_t)p.n * p.C};
-  const cuuint64_t strides[1] = {(cuuint64_t)p.HW * 4};
-  const cuuint32_t box[2] = {(cuuint32_t)c.PSw, (cuuint32_t)c.nchm};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(x), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 }  // namespace
 
 bool tc_wgrad_supported(const Problem &p) {
@@ -673,7 +639,8 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   WgCfg c = wg_cfg(p, device_sm_count());
   CUtensorMap xmap;
   std::memset(&xmap, 0, sizeof(xmap));
-  if (c.tma && !encode_x_map(p, c, x, &xmap)) c.tma = 0;  // per-channel bulk copies instead (same layout)
+  if (c.tma && !encode_planes_map(x, p.HW, (int64_t)p.n * p.C, c.PSw, c.nchm, &xmap))
+    c.tma = 0;  // per-channel bulk copies instead (same layout)
   int *status = device_status_ptr();
   if (!status) {
     set_last_error("could not resolve the device status word");
