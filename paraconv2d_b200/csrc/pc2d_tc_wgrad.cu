@@ -82,8 +82,20 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   c.cpi = ceil_div(p.PQ, kChunk);
   c.chunks = (int64_t)p.n * c.cpi;
   const int64_t per = (int64_t)c.nNR * c.nmb;
-  int64_t seg = c.chunks * per / std::max<int64_t>(1, 2 * sms);
-  c.SEG = (int)std::max<int64_t>(4, std::min<int64_t>(kMaxSeg, seg));
+  // Segment length: the one whose critical path (rounds of items per SM x
+  // chunks per item, plus a per-item cost of ~2 chunks for the drain and
+  // the hand-over) is shortest.
+  c.SEG = kMaxSeg;
+  int64_t best = -1;
+  for (int seg = 4; seg <= kMaxSeg; ++seg) {
+    const int64_t items = (c.chunks + seg - 1) / seg * per;
+    const int64_t rounds = (items + std::max(1, sms) - 1) / std::max(1, sms);
+    const int64_t cost = rounds * (seg + 2);
+    if (best < 0 || cost < best) {
+      best = cost;
+      c.SEG = seg;
+    }
+  }
   c.nseg = (c.chunks + c.SEG - 1) / c.SEG;
   c.items = c.nseg * per;
   c.bstage = (uint32_t)(2 * c.NR * 128);
