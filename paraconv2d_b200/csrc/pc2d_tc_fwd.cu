@@ -10,18 +10,20 @@
 // pixels of one image per tile, N = [H;P] rows of a channel block (2*NB,
 // NB <= 64) and K = the window (C*k0*k1), swept 32 at a time.
 //
-// Data movement per 32-K stage (3 stages in flight):
-//   - the loader warp issues 1-D bulk copies of (a) the pre-split weights of
-//     the stage ([H;P] hi and lo, 128-byte-swizzled K-major, written once per
-//     call by a prep kernel) and (b) the input "halo" of the stage: for each
-//     channel the stage's window touches, the contiguous run of input rows
-//     the tile reads (16-byte rounded), all completing on one barrier;
+// Data movement per stage (64 K = two 32-K sub-stages with 2 stages in flight
+// when the halo is one tensor copy, else 32 K with 4 in flight):
+//   - the loader warp copies (a) the pre-split weights of the stage ([H;P] hi
+//     and lo of two 32-K blocks, 128-byte-swizzled K-major, written once per
+//     call by a prep kernel; one bulk copy) and (b) the input "halo" of the
+//     stage: for each channel the stage's window touches, the run of input
+//     rows the tile reads (one 2-D tensor copy, or 16-byte-rounded bulk
+//     copies per channel), all completing on one barrier;
 //   - four producer warps (one TMEM lane = one output pixel per thread)
-//     gather the 32 window values of their pixel from the halo in shared
+//     gather the 64 window values of their pixel from the halo in shared
 //     memory, split them into tf32 hi + lo, accumulate S2, and tcgen05.st
 //     the hi and lo slices into the stage's TMEM columns (A operand);
-//   - one thread of the MMA warp issues, per 8-wide K step, the three
-//     products Ahi*Bhi + Alo*Bhi + Ahi*Blo as MMAs with N = 2NB.
+//   - one elected thread of the MMA warp issues, per 8-wide K step, the
+//     three products Ahi*Bhi + Alo*Bhi + Ahi*Blo as MMAs with N = 2NB.
 //
 // Accumulation: the tensor core's fp32 accumulation loses up to one unit in
 // the last place per instruction, so a long K sweep into one accumulator
@@ -29,8 +31,9 @@
 // fresh partial sum (enable_input_d = 0) in one of two [H | P] slots of TMEM,
 // and the epilogue warps drain each partial into fp32 registers
 // (round-to-nearest adds) while the MMAs fill the other slot.
-//   TMEM columns: slots [0,128) [128,256); A stages [256,448) as
-//   3 x (hi 32 | lo 32).
+//   TMEM columns: slots [0,128) [128,256); A stages [256,512): 2 x (hi 32 |
+//   lo 32 | hi 32 | lo 32) with 64-K stages, 4 x (hi 32 | lo 32) with 32-K
+//   stages.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over work items):
 //   warps 0-3 producers, 4-7 epilogue, 8 MMA issuer (and TMEM owner),
@@ -52,30 +55,32 @@ using tc::warp_wait;
 using tc::kWaitNs;
 
 constexpr int kTileM = 128;
-constexpr int kKS = 32;          // K per stage (one 128-byte swizzle row of tf32)
-constexpr int kMaxStages = 4;    // stages in flight (4, or 3 when shared memory is short)
+constexpr int kKS = 32;          // K per sub-stage (one 128-byte swizzle row of tf32)
+constexpr int kMaxStages = 4;    // barrier sets; SUB-K stages in flight = 4 / SUB
+constexpr int kMaxCh = 64;       // channel planes a stage may touch
 constexpr int kSlots = 2;        // partial-sum slots in TMEM
-constexpr int kGroupStages = 2;  // stages per partial sum (64 K)
 constexpr int kMaxNB = 64;
 constexpr int kMaxD = 8192;
 constexpr int kFwdThreads = 320;
 constexpr int kMinSmem = 120 * 1024;  // keeps one CTA per SM (it owns all 512 TMEM columns)
 constexpr int kSmemLimit = 227 * 1024;
-constexpr uint32_t kColA = 256;       // A stages at 256 + 64 * stage: hi 32, lo 32
+constexpr uint32_t kColA = 256;       // A stages at 256 + 64 * SUB * stage: (hi 32, lo 32) per sub-stage
 
 struct FwdCfg {
   int ncb;          // channel blocks
   int NB;           // channels per block (multiple of 16, <= 64)
   int N;            // rows of a B stage = 2*NB ([H;P])
-  int nK;           // 32-wide K stages per tile
-  int nst;          // stages in flight
-  int nGroups;      // partial sums per tile
+  int sub;          // 32-K sub-stages per stage (2 with a single-copy halo, else 1)
+  int nK;           // stages per tile (= partial sums per tile)
+  int nKB;          // 32-wide K blocks of the weight layout (= sub * nK)
+  int nst;          // stages in flight (4 / sub)
+  int nGroups;      // partial sums (64 K each) per tile
   int tpi;          // tiles per image
   int64_t tiles;    // 128-pixel tiles (never crossing an image)
   int64_t items;    // tiles * ncb
   int PS;           // halo plane stride in floats (multiple of 4)
-  int nchs;         // channels a stage touches at most (<= 32)
-  uint32_t bstage;  // B bytes per stage (hi + lo)
+  int nchs;         // channels a stage touches at most
+  uint32_t bstage;  // B bytes of one 32-K block (hi + lo); a stage holds SUB blocks
   uint32_t sstage;  // shared bytes per stage (B + halo, multiple of 1024)
   int tma;          // 1: a stage's halo is one 2-D tensor copy [nchs planes][PS floats]
 };
@@ -86,46 +91,49 @@ FwdCfg fwd_cfg(const Problem &p) {
   const int nb = ceil_div(p.m, c.ncb);
   c.NB = (nb + 15) / 16 * 16;
   c.N = 2 * c.NB;
-  c.nK = ceil_div(p.d, kKS);
-  c.nGroups = ceil_div(c.nK, kGroupStages);
-  c.tpi = ceil_div(p.PQ, kTileM);
-  c.tiles = (int64_t)p.n * c.tpi;
-  c.items = c.tiles * c.ncb;
   // output rows a run of 128 consecutive pixels of one image can touch
-  const int orow = std::min<int64_t>(p.P, (p.Q + kTileM - 2) / p.Q + 1);
-  const int R = (orow - 1) * p.s0 + (p.k0 - 1) * p.dl0 + 1;
-  c.PS = (int)(((int64_t)R * p.W + 8 + 3) / 4 * 4);
-  c.nchs = 0;
-  for (int kq = 0; kq < c.nK; ++kq) {
-    const int clo = (int)(((int64_t)kq * kKS) / p.T);
-    const int chi = (int)(std::min<int64_t>((int64_t)kq * kKS + kKS - 1, p.d - 1) / p.T);
-    c.nchs = std::max(c.nchs, chi - clo + 1);
+  {
+    const int orow = std::min<int64_t>(p.P, (p.Q + kTileM - 2) / p.Q + 1);
+    const int R = (orow - 1) * p.s0 + (p.k0 - 1) * p.dl0 + 1;
+    c.PS = (int)(((int64_t)R * p.W + 8 + 3) / 4 * 4);
   }
-  c.bstage = (uint32_t)(2 * c.N * 128);
-  const size_t hb = align_up((size_t)c.nchs * c.PS * 4, 1024);
-  c.sstage = (uint32_t)(c.bstage + hb);
-  c.nst = kMaxStages;
   // one tensor copy per stage: channel planes 16-byte strided, the plane
   // stride PS (from the 16-byte boundary at or below the tile's first input
   // element) at most 256 floats
   c.tma = (p.HW % 4 == 0 && c.PS <= 256 && (int64_t)p.n * p.C < ((int64_t)1 << 31)) ? 1 : 0;
+  // 64-K stages halve the hand-offs per K when a tile has many of them; with
+  // a short window (few stages per tile) four 32-K stages in flight hide the
+  // copies better
+  c.sub = p.d >= 256 ? 2 : 1;
+  c.nst = kMaxStages / c.sub;
+  c.nK = ceil_div(p.d, kKS * c.sub);
+  c.nKB = c.nK * c.sub;
+  c.nGroups = ceil_div(c.nK, 2 / c.sub);
+  c.tpi = ceil_div(p.PQ, kTileM);
+  c.tiles = (int64_t)p.n * c.tpi;
+  c.items = c.tiles * c.ncb;
+  c.nchs = 0;
+  const int kst = kKS * c.sub;
+  for (int kq = 0; kq < c.nK; ++kq) {
+    const int clo = (int)(((int64_t)kq * kst) / p.T);
+    const int chi = (int)(std::min<int64_t>((int64_t)kq * kst + kst - 1, p.d - 1) / p.T);
+    c.nchs = std::max(c.nchs, chi - clo + 1);
+  }
+  c.bstage = (uint32_t)(2 * c.N * 128);
+  const size_t hb = align_up((size_t)c.nchs * c.PS * 4, 1024);
+  c.sstage = (uint32_t)(c.sub * c.bstage + hb);
   return c;
 }
 
-inline size_t fwd_bsplit_bytes(const FwdCfg &c) { return (size_t)c.ncb * c.nK * c.bstage; }
+inline size_t fwd_bsplit_bytes(const FwdCfg &c) { return (size_t)c.ncb * c.nKB * c.bstage; }
 inline size_t fwd_smem_bytes(const Problem &p, const FwdCfg &c) {
-  size_t s = 1024 + (size_t)c.nst * c.sstage + (size_t)c.nK * kKS * 8 + (size_t)kMaxStages * kKS * 4 +
-             (size_t)kMaxStages * 32 * 4 + 2 * kTileM * 4 + 24 * 8 + 64;
+  size_t s = 1024 + (size_t)c.nst * c.sstage + (size_t)c.nKB * kKS * 8 + (size_t)kMaxStages * kKS * 4 +
+             (size_t)kMaxStages * kMaxCh * 4 + 2 * kTileM * 4 + 24 * 8 + 64;
   (void)p;
   return std::max<size_t>(s, kMinSmem);
 }
 
-// Picks 4 stages when they fit in shared memory, else 3.
-inline FwdCfg fwd_cfg_fit(const Problem &p) {
-  FwdCfg c = fwd_cfg(p);
-  if (fwd_smem_bytes(p, c) > (size_t)kSmemLimit) c.nst = 3;
-  return c;
-}
+inline FwdCfg fwd_cfg_fit(const Problem &p) { return fwd_cfg(p); }
 
 // Splits [H;P] of channel block cb into hi/lo tf32 halves in the swizzled
 // K-major layout the MMA reads: block (cb, kc) = [hi: N rows][lo: N rows],
@@ -134,7 +142,7 @@ inline FwdCfg fwd_cfg_fit(const Problem &p) {
 // and K >= d are zero.
 __global__ void tc_fwd_prep_weights(const float *__restrict__ pars, Problem p, FwdCfg c, float *__restrict__ wsB) {
   const int kc = blockIdx.x, cb = blockIdx.y;
-  float *blk = wsB + ((int64_t)cb * c.nK + kc) * 2 * c.N * 32;
+  float *blk = wsB + ((int64_t)cb * c.nKB + kc) * 2 * c.N * 32;
   const float *h = pars + p.m;
   const float *pp = h + (int64_t)p.m * p.d;
   for (int e = threadIdx.x; e < c.N * 32; e += blockDim.x) {
@@ -196,17 +204,17 @@ __device__ __forceinline__ TileGeo tile_geo(const Problem &p, const FwdCfg &c, i
 }
 
 struct Smem {
-  uint8_t *stage;   // nst x [B hi | B lo | halo planes]
+  uint8_t *stage;   // nst x [SUB x (B hi | B lo) | halo planes]
   int2 *koff;       // per K: (channel, tap offset row*W + col), channel -1 past d
-  int *offs;        // [stage][32] halo offset of each K of the stage (-1 = zero)
-  int *lead;        // [stage][32] floats before each halo plane's first element
+  int *offs;        // [stage][32 SUB] halo offset of each K of the stage (-1 = zero)
+  int *lead;        // [stage][64] floats before each halo plane's first element
   float *s2buf;     // [tile buffer 2][128]
   uint64_t *full, *a_full, *s_empty, *gr_full, *gr_empty, *s2_full, *s2_empty, *final_bar;
   uint32_t *tmem_holder;
   volatile int *abort_flag;
 };
 
-template <int NB>
+template <int NB, int SUB>
 __global__ void __launch_bounds__(kFwdThreads, 1)
 tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, const float *__restrict__ wsB,
                   const float *__restrict__ cj, float factor, Problem p, FwdCfg c,
@@ -219,9 +227,10 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   const int nst = c.nst;
   S.stage = base;
   S.koff = reinterpret_cast<int2 *>(base + (size_t)nst * c.sstage);
-  S.offs = reinterpret_cast<int *>(S.koff + c.nK * kKS);
+  constexpr int kKStage = kKS * SUB;  // K per stage = one partial sum
+  S.offs = reinterpret_cast<int *>(S.koff + c.nK * kKStage);
   S.lead = S.offs + kMaxStages * kKS;
-  S.s2buf = reinterpret_cast<float *>(S.lead + kMaxStages * 32);
+  S.s2buf = reinterpret_cast<float *>(S.lead + kMaxStages * kMaxCh);
   uint64_t *bars = reinterpret_cast<uint64_t *>(
       (reinterpret_cast<uintptr_t>(S.s2buf + 2 * kTileM) + 7) & ~(uintptr_t)7);
   S.full = bars;            // [4] halo + B + offsets landed (loader expect_tx)
@@ -235,7 +244,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   S.tmem_holder = reinterpret_cast<uint32_t *>(bars + 21);
   S.abort_flag = reinterpret_cast<volatile int *>(S.tmem_holder + 1);
 
-  for (int k = threadIdx.x; k < c.nK * kKS; k += blockDim.x) {
+  for (int k = threadIdx.x; k < c.nK * kKStage; k += blockDim.x) {
     int2 v = make_int2(-1, 0);
     if (k < p.d) {
       const int ch = k / p.T, tap = k - ch * p.T;
@@ -294,32 +303,35 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           break;
         }
         tc_fence_after();
-        const float *halo = reinterpret_cast<const float *>(S.stage + (size_t)st * c.sstage + c.bstage);
-        const int4 *offs = reinterpret_cast<const int4 *>(S.offs + st * kKS);
-        int o[32];
+        const float *halo = reinterpret_cast<const float *>(S.stage + (size_t)st * c.sstage + SUB * c.bstage);
 #pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) {
-          const int4 t4 = offs[q4];
-          o[4 * q4 + 0] = t4.x;
-          o[4 * q4 + 1] = t4.y;
-          o[4 * q4 + 2] = t4.z;
-          o[4 * q4 + 3] = t4.w;
+        for (int sub = 0; sub < SUB; ++sub) {
+          const int4 *offs = reinterpret_cast<const int4 *>(S.offs + st * kKStage + sub * kKS);
+          int o[32];
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const int4 t4 = offs[q4];
+            o[4 * q4 + 0] = t4.x;
+            o[4 * q4 + 1] = t4.y;
+            o[4 * q4 + 2] = t4.z;
+            o[4 * q4 + 3] = t4.w;
+          }
+          float v[32];
+#pragma unroll
+          for (int kk = 0; kk < 32; ++kk) v[kk] = (valid && o[kk] >= 0) ? halo[o[kk] + poff] : 0.f;
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int kk = 0; kk < 32; ++kk) {
+            s2 = fmaf(v[kk], v[kk], s2);
+            hi[kk] = tf32_hi_bits(v[kk]);
+            lo[kk] = __float_as_uint(v[kk] - __uint_as_float(hi[kk]));
+          }
+          const uint32_t acol = tmem + lane_off + kColA + st * (SUB * 64) + sub * 64;
+          tmem_st16(acol, *reinterpret_cast<const uint32_t(*)[16]>(&hi[0]));
+          tmem_st16(acol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&hi[16]));
+          tmem_st16(acol + 32, *reinterpret_cast<const uint32_t(*)[16]>(&lo[0]));
+          tmem_st16(acol + 48, *reinterpret_cast<const uint32_t(*)[16]>(&lo[16]));
         }
-        float v[32];
-#pragma unroll
-        for (int kk = 0; kk < 32; ++kk) v[kk] = (valid && o[kk] >= 0) ? halo[o[kk] + poff] : 0.f;
-        uint32_t hi[32], lo[32];
-#pragma unroll
-        for (int kk = 0; kk < 32; ++kk) {
-          s2 = fmaf(v[kk], v[kk], s2);
-          hi[kk] = tf32_hi_bits(v[kk]);
-          lo[kk] = __float_as_uint(v[kk] - __uint_as_float(hi[kk]));
-        }
-        const uint32_t acol = tmem + lane_off + kColA + st * 64;
-        tmem_st16(acol, *reinterpret_cast<const uint32_t(*)[16]>(&hi[0]));
-        tmem_st16(acol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&hi[16]));
-        tmem_st16(acol + 32, *reinterpret_cast<const uint32_t(*)[16]>(&lo[0]));
-        tmem_st16(acol + 48, *reinterpret_cast<const uint32_t(*)[16]>(&lo[16]));
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&S.a_full[st]);
@@ -355,18 +367,35 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
         }
         tc_fence_after();
         const uint32_t dcol = tmem + lane_off + slot * 128;
+        if constexpr (NB == 48) {
+          // 16 columns of H and of P at a time: with 96 accumulators live,
+          // 32-column loads would spill
 #pragma unroll
-        for (int jc = 0; jc < NB; jc += 32) {
-          uint32_t hv[32], pv[32];
-          tmem_ld32_nowait(dcol + jc, hv);
-          tmem_ld32_nowait(dcol + NB + jc, pv);
-          tmem_ld_wait_tie(hv);
-          tmem_ld_wait_tie(pv);
+          for (int jc = 0; jc < NB; jc += 16) {
+            uint32_t hv[16], pv[16];
+            tmem_ld16_nowait(dcol + jc, hv);
+            tmem_ld16_nowait(dcol + NB + jc, pv);
+            tmem_ld_wait_tie(hv, pv);
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            if (jc + jj < NB) {
+            for (int jj = 0; jj < 16; ++jj) {
               hacc[jc + jj] += __uint_as_float(hv[jj]);
               pacc[jc + jj] += __uint_as_float(pv[jj]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int jc = 0; jc < NB; jc += 32) {
+            uint32_t hv[32], pv[32];
+            tmem_ld32_nowait(dcol + jc, hv);
+            tmem_ld32_nowait(dcol + NB + jc, pv);
+            tmem_ld_wait_tie(hv);
+            tmem_ld_wait_tie(pv);
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+              if (jc + jj < NB) {
+                hacc[jc + jj] += __uint_as_float(hv[jj]);
+                pacc[jc + jj] += __uint_as_float(pv[jj]);
+              }
             }
           }
         }
@@ -402,19 +431,19 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
     const uint32_t idesc = idesc_tf32(kTileM, 2 * NB);
     constexpr uint32_t kBlo = 2 * NB * 128;  // bytes of the hi rows of a B stage
     const uint32_t stage_addr = smem_u32(S.stage);
+    constexpr int kGS = 2 / SUB;  // stages per partial sum (64 K)
     uint32_t it = 0, grp = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
-      uint32_t dcol = 0, slot = 0;
+      uint32_t slot = 0;
       for (int kq = 0; kq < c.nK; ++kq, ++it) {
-        const bool gstart = (kq % kGroupStages) == 0;
-        const bool gend = (kq % kGroupStages) == kGroupStages - 1 || kq == c.nK - 1;
+        const bool gstart = (kq % kGS) == 0;
+        const bool gend = (kq % kGS) == kGS - 1 || kq == c.nK - 1;
         if (gstart) {
           slot = grp % kSlots;
           if (!warp_wait(&S.gr_empty[slot], ((grp / kSlots) & 1) ^ 1, S.abort_flag)) {
             ok = false;
             break;
           }
-          dcol = tmem + slot * 128;
         }
         const uint32_t st = it % nst, ph = (it / nst) & 1;
         if (!warp_wait(&S.a_full[st], ph, S.abort_flag)) {
@@ -423,17 +452,23 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
         }
         tc_fence_after();
         // straight-line issue from one elected lane, operands formed outside
-        const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
-        const uint32_t bhi0 = stage_addr + st * c.sstage;  // [H;P] rows, hi
+        const uint32_t dcol = tmem + slot * 128;
+        const uint32_t acol = tmem + kColA + st * (SUB * 64);
+        const uint32_t bst = stage_addr + st * c.sstage;  // per sub-stage: [H;P] hi rows, then lo rows
+        const uint32_t bsub = c.bstage;
         const uint32_t acc0 = gstart ? 0u : 1u;
         if (elect_one()) {
 #pragma unroll
-          for (int ks = 0; ks < kKS / 8; ++ks) {
-            const uint32_t bhi = bhi0 + ks * 32;
-            const uint32_t blo = bhi + kBlo;  // lo
-            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(bhi), idesc, ks == 0 ? acc0 : 1u);
-            mma_tf32_ts(dcol, alo + ks * 8, sdesc_kmajor_sw128(bhi), idesc, 1u);
-            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(blo), idesc, 1u);
+          for (int sub = 0; sub < SUB; ++sub) {
+#pragma unroll
+            for (int ks = 0; ks < kKS / 8; ++ks) {
+              const uint32_t ahi = acol + sub * 64 + ks * 8, alo = ahi + 32;
+              const uint32_t bhi = bst + sub * bsub + ks * 32;
+              const uint32_t blo = bhi + kBlo;
+              mma_tf32_ts(dcol, ahi, sdesc_kmajor_sw128(bhi), idesc, (sub == 0 && ks == 0) ? acc0 : 1u);
+              mma_tf32_ts(dcol, alo, sdesc_kmajor_sw128(bhi), idesc, 1u);
+              mma_tf32_ts(dcol, ahi, sdesc_kmajor_sw128(blo), idesc, 1u);
+            }
           }
           tc_commit(&S.s_empty[st]);
           if (gend) tc_commit(&S.gr_full[slot]);
@@ -461,30 +496,35 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           ok = false;
           break;
         }
-        const int clo = S.koff[kq * kKS].x;
+        const int clo = S.koff[kq * kKStage].x;
         uint8_t *sbase = S.stage + (size_t)st * c.sstage;
+        uint8_t *hbase = sbase + SUB * c.bstage;
+        const float *bsrc = wsB + ((int64_t)cb * c.nKB + (int64_t)kq * SUB) * 2 * c.N * 32;
         if (c.tma) {
           // one tensor copy: planes clo .. clo+nchs-1 of image n, PS floats
           // each from the 16-byte boundary at or below the tile's first input
           // element (zero past the end of the tensor)
           const int xo = tg.ir0 * p.W, x0 = xo & ~3, ld = xo - x0;
-          const int2 ko = S.koff[kq * kKS + lane];
-          S.offs[st * kKS + lane] = ko.x >= 0 ? (ko.x - clo) * c.PS + ld + ko.y : -1;
+#pragma unroll
+          for (int e = 0; e < kKStage / 32; ++e) {
+            const int2 ko = S.koff[kq * kKStage + lane + 32 * e];
+            S.offs[st * kKStage + lane + 32 * e] = ko.x >= 0 ? (ko.x - clo) * c.PS + ld + ko.y : -1;
+          }
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive_expect_tx(&S.full[st], c.bstage + (uint32_t)(c.nchs * c.PS * 4));
-            bulk_g2s(sbase, wsB + ((int64_t)cb * c.nK + kq) * 2 * c.N * 32, c.bstage, &S.full[st]);
-            tma_load_2d(sbase + c.bstage, &xmap, x0, (int)(tg.n * p.C + clo), &S.full[st]);
+            mbar_arrive_expect_tx(&S.full[st], SUB * c.bstage + (uint32_t)(c.nchs * c.PS * 4));
+            bulk_g2s(sbase, bsrc, SUB * c.bstage, &S.full[st]);
+            tma_load_2d(hbase, &xmap, x0, (int)(tg.n * p.C + clo), &S.full[st]);
           }
           __syncwarp();
           continue;
         }
-        // Channel planes of the stage (one lane each): 16-byte-rounded spans,
-        // their leads and the total byte count.
+        // Channel planes of the stage (lanes, two rounds): 16-byte-rounded
+        // spans, their leads and the total byte count.
         int chi = clo;
 #pragma unroll 1
-        for (int kk = kKS - 1; kk >= 0; --kk) {
-          const int ch = S.koff[kq * kKS + kk].x;
+        for (int kk = kKStage - 1; kk >= 0; --kk) {
+          const int ch = S.koff[kq * kKStage + kk].x;
           if (ch >= 0) {
             chi = ch;
             break;
@@ -492,28 +532,31 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
         }
         const int nch = chi - clo + 1;
         uint32_t bytes = 0;
-        tc::BulkSpan sp{};
-        if (lane < nch) {
-          sp = tc::bulk_span(ximg + (int64_t)(clo + lane) * p.HW, run);
-          S.lead[st * 32 + lane] = sp.lead;
-          bytes = sp.bytes;
+        for (int ci = lane; ci < nch; ci += 32) {
+          const tc::BulkSpan sp = tc::bulk_span(ximg + (int64_t)(clo + ci) * p.HW, run);
+          S.lead[st * kMaxCh + ci] = sp.lead;
+          bytes += sp.bytes;
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
         __syncwarp();
         // Offset of every K of the stage inside the halo: plane, lead, tap.
-        {
-          const int2 ko = S.koff[kq * kKS + lane];
-          S.offs[st * kKS + lane] =
-              ko.x >= 0 ? (ko.x - clo) * c.PS + S.lead[st * 32 + (ko.x - clo)] + ko.y : -1;
+#pragma unroll
+        for (int e = 0; e < kKStage / 32; ++e) {
+          const int2 ko = S.koff[kq * kKStage + lane + 32 * e];
+          S.offs[st * kKStage + lane + 32 * e] =
+              ko.x >= 0 ? (ko.x - clo) * c.PS + S.lead[st * kMaxCh + (ko.x - clo)] + ko.y : -1;
         }
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive_expect_tx(&S.full[st], c.bstage + bytes);
-          bulk_g2s(sbase, wsB + ((int64_t)cb * c.nK + kq) * 2 * c.N * 32, c.bstage, &S.full[st]);
+          mbar_arrive_expect_tx(&S.full[st], SUB * c.bstage + bytes);
+          bulk_g2s(sbase, bsrc, SUB * c.bstage, &S.full[st]);
         }
         __syncwarp();
-        if (lane < nch) bulk_g2s(sbase + c.bstage + (size_t)lane * c.PS * 4, sp.src, sp.bytes, &S.full[st]);
+        for (int ci = lane; ci < nch; ci += 32) {
+          const tc::BulkSpan sp = tc::bulk_span(ximg + (int64_t)(clo + ci) * p.HW, run);
+          bulk_g2s(hbase + (size_t)ci * c.PS * 4, sp.src, sp.bytes, &S.full[st]);
+        }
         __syncwarp();
       }
     }
@@ -549,8 +592,32 @@ __global__ void selftest_wait_kernel(unsigned int timeout_us, int *status) {
 }
 
 std::mutex g_attr_mutex;
-bool g_attr_set[64][4] = {};
+bool g_attr_set[64][8] = {};
 int g_sm_count[64] = {0};
+
+template <int NB, int SUB>
+int launch_forward_sub(const Problem &p, const FwdCfg &c, const CUtensorMap &xmap, const float *x, const float *pars,
+                       const float *wsB, const float *cj, float factor, float *out, float *hsum, int *status,
+                       cudaStream_t stream) {
+  int dev = 0;
+  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    const int slot = (NB / 16 - 1) * 2 + (SUB - 1);
+    if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot]) {
+      PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_forward_kernel<NB, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           227 * 1024));
+      g_attr_set[dev][slot] = true;
+    }
+  }
+  const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
+  timing_begin(K_FORWARD, stream);
+  tc_forward_kernel<NB, SUB><<<grid, kFwdThreads, fwd_smem_bytes(p, c), stream>>>(x, pars, wsB, cj, factor, p, c, xmap,
+                                                                               out, hsum, status);
+  timing_end(K_FORWARD, stream);
+  PC2D_LAUNCH_CHECK("tc_forward_kernel");
+  return PC2D_OK;
+}
 
 template <int NB>
 int launch_forward(const Problem &p, FwdCfg c, const float *x, const float *pars, const float *wsB,
@@ -559,23 +626,8 @@ int launch_forward(const Problem &p, FwdCfg c, const float *x, const float *pars
   std::memset(&xmap, 0, sizeof(xmap));
   if (c.tma && !encode_planes_map(x, p.HW, (int64_t)p.n * p.C, c.PS, c.nchs, &xmap))
     c.tma = 0;  // per-channel bulk copies instead (same layout)
-  int dev = 0;
-  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
-  {
-    std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (dev >= 0 && dev < 64 && !g_attr_set[dev][NB / 16 - 1]) {
-      PC2D_CUDA_CHECK(
-          cudaFuncSetAttribute(tc_forward_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-      g_attr_set[dev][NB / 16 - 1] = true;
-    }
-  }
-  const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
-  timing_begin(K_FORWARD, stream);
-  tc_forward_kernel<NB><<<grid, kFwdThreads, fwd_smem_bytes(p, c), stream>>>(x, pars, wsB, cj, factor, p, c, xmap, out,
-                                                                          hsum, status);
-  timing_end(K_FORWARD, stream);
-  PC2D_LAUNCH_CHECK("tc_forward_kernel");
-  return PC2D_OK;
+  if (c.sub == 2) return launch_forward_sub<NB, 2>(p, c, xmap, x, pars, wsB, cj, factor, out, hsum, status, stream);
+  return launch_forward_sub<NB, 1>(p, c, xmap, x, pars, wsB, cj, factor, out, hsum, status, stream);
 }
 
 }  // namespace
@@ -629,7 +681,7 @@ int device_sm_count() {
 bool tc_forward_supported(const Problem &p) {
   if (p.m < 1 || p.d > kMaxD || p.CHW >= ((int64_t)1 << 31) || p.NPQ <= 0 || p.PQ >= ((int64_t)1 << 30)) return false;
   const FwdCfg c = fwd_cfg_fit(p);
-  return c.nchs <= 32 && fwd_smem_bytes(p, c) <= (size_t)kSmemLimit;
+  return c.nchs <= kMaxCh && fwd_smem_bytes(p, c) <= (size_t)kSmemLimit;
 }
 
 size_t tc_forward_workspace(const Problem &p) {
@@ -647,7 +699,7 @@ int tc_forward(const Problem &p, const float *x, const float *pars, double facto
   }
   float *wsB = reinterpret_cast<float *>(ws);
   float *cj = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + align_up(fwd_bsplit_bytes(c), 256));
-  tc_fwd_prep_weights<<<dim3(c.nK, c.ncb), 256, 0, stream>>>(pars, p, c, wsB);
+  tc_fwd_prep_weights<<<dim3(c.nKB, c.ncb), 256, 0, stream>>>(pars, p, c, wsB);
   PC2D_LAUNCH_CHECK("tc_fwd_prep_weights");
   tc_fwd_prep_consts<<<ceil_div(c.ncb * c.NB, 8), 256, 0, stream>>>(pars, p, c, cj);
   PC2D_LAUNCH_CHECK("tc_fwd_prep_consts");
