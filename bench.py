@@ -462,10 +462,10 @@ def run_ours(args):
 
 def launches_per_step(lib, ktimes, steps):
     """Our kernel launches per device-resident step, from the timed main
-    kernels: tcgen05 forward = 2 prep kernels + the main kernel; tcgen05
+    kernels: tcgen05 forward = 1 prep kernel + the main kernel; tcgen05
     dgrad = 1 prep + main; tcgen05 wgrad = main + fixed-order reduction;
     CUDA-core forward = 1; CUDA-core dgrad = 1; CUDA-core wgrad = 2."""
-    per_main = {"forward": 3, "dgrad": 2, "wgrad": 2, "simt_forward": 1, "simt_dgrad": 1, "simt_wgrad": 2}
+    per_main = {"forward": 2, "dgrad": 2, "wgrad": 2, "simt_forward": 1, "simt_dgrad": 1, "simt_wgrad": 2}
     total = sum(per_main[k] * v[1] for k, v in ktimes.items())
     return total // max(1, steps)
 

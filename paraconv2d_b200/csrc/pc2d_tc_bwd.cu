@@ -160,14 +160,17 @@ inline size_t dg_smem_bytes(const DgCfg &c) {
 // tf32 hi/lo, 128-byte-swizzled K-major: rows = channels (hi block then lo
 // block), K element kk = (j_local = kk/2, w = kk%2) holds h[j][c][tap]
 // (w = 0, multiplies g*hsum) or p[j][c][tap] (w = 1, multiplies g).
-__global__ void tc_dg_prep_weights(const float *__restrict__ pars, Problem p, DgCfg c, float *__restrict__ wsB) {
+// Grid (nK, ncb, NC / 8): each thread block writes 8 channel rows of one
+// (j-block, tap) block.
+__global__ void __launch_bounds__(256) tc_dg_prep_weights(const float *__restrict__ pars, Problem p, DgCfg c,
+                                                          float *__restrict__ wsB) {
   const int kq = blockIdx.x, cb = blockIdx.y;
   const int jb = kq / p.T, tap = kq - (kq / p.T) * p.T;
   float *blk = wsB + ((int64_t)cb * c.nK + kq) * 2 * c.NC * 32;
   const float *h = pars + p.m;
   const float *pp = h + (int64_t)p.m * p.d;
-  for (int e = threadIdx.x; e < c.NC * 32; e += blockDim.x) {
-    const int r = e / 32, kk = e % 32;
+  for (int e = threadIdx.x; e < 8 * 32; e += blockDim.x) {
+    const int r = blockIdx.z * 8 + e / 32, kk = e % 32;
     const int ch = cb * c.NC + r;
     const int j = jb * kJB + kk / 2;
     float v = 0.f;
@@ -681,7 +684,7 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
     }
     const DgCfg c = dg_cfg(p);
     float *wsB = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + wscr);
-    tc_dg_prep_weights<<<dim3(c.nK, c.ncb), 256, 0, stream>>>(pars, p, c, wsB);
+    tc_dg_prep_weights<<<dim3(c.nK, c.ncb, c.NC / 8), 256, 0, stream>>>(pars, p, c, wsB);
     PC2D_LAUNCH_CHECK("tc_dg_prep_weights");
     int st = PC2D_OK;
     switch (c.NC) {

@@ -135,33 +135,41 @@ inline size_t fwd_smem_bytes(const Problem &p, const FwdCfg &c) {
 
 inline FwdCfg fwd_cfg_fit(const Problem &p) { return fwd_cfg(p); }
 
-// Splits [H;P] of channel block cb into hi/lo tf32 halves in the swizzled
-// K-major layout the MMA reads: block (cb, kc) = [hi: N rows][lo: N rows],
-// each row 32 floats of K with 16-byte chunk c stored at c ^ (row % 8).
-// Rows 0..NB-1 are H of channels cb*NB.., rows NB..2NB-1 are P; channels >= m
-// and K >= d are zero.
-__global__ void tc_fwd_prep_weights(const float *__restrict__ pars, Problem p, FwdCfg c, float *__restrict__ wsB) {
-  const int kc = blockIdx.x, cb = blockIdx.y;
-  float *blk = wsB + ((int64_t)cb * c.nKB + kc) * 2 * c.N * 32;
-  const float *h = pars + p.m;
-  const float *pp = h + (int64_t)p.m * p.d;
-  for (int e = threadIdx.x; e < c.N * 32; e += blockDim.x) {
-    const int r = e / 32, kk = e % 32;
-    const int half = r / c.NB;
-    const int j = cb * c.NB + (r - half * c.NB);
-    const int64_t k = (int64_t)kc * 32 + kk;
-    float v = 0.f;
-    if (j < p.m && k < p.d) v = (half == 0 ? h : pp)[(int64_t)j * p.d + k];
-    const float hi = __uint_as_float(tf32_hi_bits(v));
-    const int pos = r * 32 + (((kk >> 2) ^ (r & 7)) << 2) + (kk & 3);
-    blk[pos] = hi;
-    blk[c.N * 32 + pos] = v - hi;
+// Per-call preparation of the forward's constant operands, one launch:
+//  - blocks [0, ncb * nKB * kPrepSplit): split [H;P] of channel block cb into
+//    hi/lo tf32 halves in the swizzled K-major layout the MMA reads: block
+//    (cb, kc) = [hi: N rows][lo: N rows], each row 32 floats of K with 16-byte
+//    chunk c stored at c ^ (row % 8).  Rows 0..NB-1 are H of channels
+//    cb*NB.., rows NB..2NB-1 are P; channels >= m and K >= d are zero.  Each
+//    thread block writes N / kPrepSplit rows of one (cb, kc) block.
+//  - the remaining blocks: cj[cb*NB + jn] = |P[j]|^2 + p0[j]^2 (fp64
+//    accumulation, one warp per channel), 0 for padded channels.
+constexpr int kPrepSplit = 8;
+__global__ void __launch_bounds__(256) tc_fwd_prep(const float *__restrict__ pars, Problem p, FwdCfg c,
+                                                   float *__restrict__ wsB, float *__restrict__ cj) {
+  const int nwb = c.ncb * c.nKB * kPrepSplit;
+  if ((int)blockIdx.x < nwb) {
+    const int sp = blockIdx.x % kPrepSplit, kc = (blockIdx.x / kPrepSplit) % c.nKB;
+    const int cb = blockIdx.x / (kPrepSplit * c.nKB);
+    float *blk = wsB + ((int64_t)cb * c.nKB + kc) * 2 * c.N * 32;
+    const float *h = pars + p.m;
+    const float *pp = h + (int64_t)p.m * p.d;
+    const int rows = c.N / kPrepSplit;  // N = 2 NB is a multiple of 32
+    for (int e = threadIdx.x; e < rows * 32; e += blockDim.x) {
+      const int r = sp * rows + e / 32, kk = e % 32;
+      const int half = r / c.NB;
+      const int j = cb * c.NB + (r - half * c.NB);
+      const int64_t k = (int64_t)kc * 32 + kk;
+      float v = 0.f;
+      if (j < p.m && k < p.d) v = (half == 0 ? h : pp)[(int64_t)j * p.d + k];
+      const float hi = __uint_as_float(tf32_hi_bits(v));
+      const int pos = r * 32 + (((kk >> 2) ^ (r & 7)) << 2) + (kk & 3);
+      blk[pos] = hi;
+      blk[c.N * 32 + pos] = v - hi;
+    }
+    return;
   }
-}
-
-// cj[cb*NB + jn] = |P[j]|^2 + p0[j]^2 (fp64 accumulation), 0 for padded channels.
-__global__ void tc_fwd_prep_consts(const float *__restrict__ pars, Problem p, FwdCfg c, float *__restrict__ cj) {
-  const int slot = blockIdx.x * 8 + threadIdx.x / 32;
+  const int slot = ((int)blockIdx.x - nwb) * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (slot >= c.ncb * c.NB) return;
   const int cb = slot / c.NB;
@@ -699,10 +707,8 @@ int tc_forward(const Problem &p, const float *x, const float *pars, double facto
   }
   float *wsB = reinterpret_cast<float *>(ws);
   float *cj = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + align_up(fwd_bsplit_bytes(c), 256));
-  tc_fwd_prep_weights<<<dim3(c.nKB, c.ncb), 256, 0, stream>>>(pars, p, c, wsB);
-  PC2D_LAUNCH_CHECK("tc_fwd_prep_weights");
-  tc_fwd_prep_consts<<<ceil_div(c.ncb * c.NB, 8), 256, 0, stream>>>(pars, p, c, cj);
-  PC2D_LAUNCH_CHECK("tc_fwd_prep_consts");
+  tc_fwd_prep<<<c.ncb * c.nKB * kPrepSplit + ceil_div(c.ncb * c.NB, 8), 256, 0, stream>>>(pars, p, c, wsB, cj);
+  PC2D_LAUNCH_CHECK("tc_fwd_prep");
   const float f = (float)factor;
   switch (c.NB) {
     case 16: return launch_forward<16>(p, c, x, pars, wsB, cj, f, out, hsum, status, stream);
