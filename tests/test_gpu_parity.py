@@ -7,6 +7,8 @@ pc2d_testutil (output/hsum elementwise 1e-5 + 1e-4|b|; gradients
 max|a-b| <= 1e-4 max|b|).  Both kernel families are checked: AUTO (tcgen05
 3xTF32 kernels where they apply) and SIMT (CUDA-core FMA).
 """
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -105,6 +107,41 @@ def test_full_size_backward_c2_vs_float64():
     dpa = backward(grad[:h].contiguous(), xp[:h].contiguous(), p, hsum[:h].contiguous(), 1.0, L.k, L.s, 1)[1]
     dpb = backward(grad[h:].contiguous(), xp[h:].contiguous(), p, hsum[h:].contiguous(), 1.0, L.k, L.s, 1)[1]
     assert maxrel_excess((dpa + dpb).cpu().numpy(), dp.cpu().numpy()) <= 1.0
+
+
+# Medium problems that take the tensor-core paths the measured workloads do
+# not: 64-K forward stages with per-channel halo copies (odd planes), 48-wide
+# channel blocks, two output-channel blocks, strided + dilated dgrad phases,
+# and the single-tensor-copy halo with 32-wide blocks.
+MEDIUM = {
+    "c40_m48_k3x5_s2x1_dl1x2_odd": dict(n=3, C=40, H=23, W=23, m=48, k=(3, 5), s=(2, 1), dl=(1, 2)),
+    "c64_m32_k3_aligned": dict(n=2, C=64, H=18, W=18, m=32, k=(3, 3), s=(1, 1), dl=(1, 1)),
+    "c48_m80_k3_s2": dict(n=2, C=48, H=21, W=21, m=80, k=(3, 3), s=(2, 2), dl=(1, 1)),
+}
+
+
+@pytest.mark.parametrize("name", sorted(MEDIUM))
+def test_medium_shapes_vs_float64(name):
+    """Forward and backward of seeded medium problems against the float64
+    torch restatement (outputs elementwise 1e-5 + 1e-4|b|, gradients
+    max|a-b| <= 1e-4 max|b|)."""
+    cfg = MEDIUM[name]
+    n, C, H, W, m = cfg["n"], cfg["C"], cfg["H"], cfg["W"], cfg["m"]
+    k, s, dl = cfg["k"], cfg["s"], cfg["dl"]
+    d = C * k[0] * k[1]
+    gen = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+    x = torch.rand(n, C, H, W, generator=gen) * 2 - 1
+    pars = torch.cat([torch.full((m,), 0.01), torch.randn(m * d, generator=gen) * 0.05,
+                      (torch.rand(m * d, generator=gen) * 2 - 1) * 0.5, torch.full((m,), 0.01)])
+    xd, pd = x.cuda(), pars.cuda()
+    with algo(PC2D_ALGO_AUTO):
+        out, hsum = forward(xd, pd, 1.0, k, s, dl)
+        g = torch.randn(out.shape, generator=gen)
+        dx, dp = backward(g.cuda(), xd, pd, hsum, 1.0, k, s, dl)
+        torch.cuda.synchronize()
+    ref_out, ref_hs, rdx, rdp = torch_reference(xd, pd, 1.0, k, s, dl, grad=g.cuda())
+    check_outputs(out.cpu().numpy(), hsum.cpu().numpy(), ref_out, ref_hs)
+    check_grads(dx.cpu().numpy(), dp.cpu().numpy(), rdx, rdp, m, d)
 
 
 @pytest.mark.parametrize("algo_name", sorted(ALGOS))
