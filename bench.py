@@ -368,11 +368,25 @@ def run_ours(args):
     g_host = grad.pin_memory()
     dp_host = torch.empty(p.numel(), dtype=torch.float32).pin_memory()
 
-    def e2e_step():
+    copy_stream = torch.cuda.Stream(dev)
+
+    def e2e_step(start_event=None):
+        # the upstream gradient crosses PCIe on a second stream, concurrently
+        # with the input copy and the forward; it starts after the step's
+        # start event, and the backward waits for it
+        if start_event is not None:
+            copy_stream.wait_event(start_event)
+        else:
+            copy_stream.wait_stream(stream)
+        with torch.cuda.stream(copy_stream):
+            gdd = g_host.to(dev, non_blocking=True)
+            g_ready = torch.cuda.Event()
+            g_ready.record(copy_stream)
+        gdd.record_stream(stream)
         xd = x_host.to(dev, non_blocking=True)
-        gdd = g_host.to(dev, non_blocking=True)
         layer.pars.grad = None
         y = layer(xd)
+        stream.wait_event(g_ready)
         y.backward(gdd)
         allreduce_e2e(layer.pars.grad)
         dp_host.copy_(layer.pars.grad, non_blocking=True)
@@ -390,7 +404,7 @@ def run_ours(args):
     for _ in range(args.steps):
         flush.zero_()
         e_s.record(stream)
-        e2e_step()
+        e2e_step(e_s)
         e_e.record(stream)
         e_e.synchronize()
         e_tot += e_s.elapsed_time(e_e) / 1e3
