@@ -20,6 +20,13 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
                 double factor, bool skip_input_grad, float *dx, float *dpars, void *ws, size_t ws_bytes,
                 cudaStream_t stream);
 
+// Input gradient of narrow inputs (C <= 8): GEMM over output pixels + col2im
+// (pc2d_tc_dgcol.cu).
+bool tc_dgcol_supported(const Problem &p);
+size_t tc_dgcol_workspace(const Problem &p);
+int tc_dgcol(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, float *dx,
+             void *ws, cudaStream_t stream);
+
 // Parameter-gradient GEMM and its reduction (pc2d_tc_wgrad.cu).
 bool tc_wgrad_supported(const Problem &p);
 size_t tc_wgrad_workspace(const Problem &p);

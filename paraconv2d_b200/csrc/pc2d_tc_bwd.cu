@@ -664,7 +664,10 @@ size_t wgrad_scratch(const Problem &p, bool skip_input_grad) {
 
 size_t tc_backward_workspace(const Problem &p, bool skip_input_grad) {
   size_t ws = wgrad_scratch(p, skip_input_grad);
-  if (!skip_input_grad && dg_supported(p)) ws += align_up(dg_bsplit_bytes(dg_cfg(p)), 256);
+  if (!skip_input_grad) {
+    if (tc_dgcol_supported(p)) ws += align_up(tc_dgcol_workspace(p), 256);
+    else if (dg_supported(p)) ws += align_up(dg_bsplit_bytes(dg_cfg(p)), 256);
+  }
   return ws;
 }
 
@@ -675,6 +678,11 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
   bool dx_done = false;
   if (skip_input_grad || p.NPQ == 0) {
     if (p.NHW > 0) PC2D_CUDA_CHECK(cudaMemsetAsync(dx, 0, sizeof(float) * (size_t)p.NHW * p.C, stream));
+    dx_done = true;
+  } else if (tc_dgcol_supported(p)) {
+    // few input channels: dense GEMM over the output pixels + col2im
+    const int st = tc_dgcol(p, grad, x, pars, hsum, dx, reinterpret_cast<char *>(ws) + wscr, stream);
+    if (st != PC2D_OK) return st;
     dx_done = true;
   } else if (dg_supported(p)) {
     int *status = device_status_ptr();

@@ -1,0 +1,477 @@
+// Input gradient of the ParaConv2d paraboloid convolution for narrow inputs
+// (few input channels), as a dense tcgen05 GEMM over the output pixels
+// followed by a col2im gather (fp32 via 3xTF32 split precision).
+//
+// The input-gradient (reference paraconv2d.cc:153-183)
+//   dx[c,y,x] = 2 * (sum_{tap, o: window(o,tap) = (y,x)}
+//                      sum_j (g*hsum)[j,o] h[j,c,tap] + g[j,o] p[j,c,tap]
+//                    - x[c,y,x] * SG[y,x]),   SG = sum_{tap,o} sum_j g[j,o]
+// splits into
+//   Y[o, (c,tap)] = sum_j (g*hsum)[j,o] h[j,c,tap] + g[j,o] p[j,c,tap]
+//   Y[o, SG]      = sum_j g[j,o]
+// a GEMM with M = 128 output pixels of one image per tile, N = C*T + 1
+// window columns (<= 192) and K = (j, {g*hsum, g}) = 2m, and
+//   dx[c,y,x] = 2 * (sum_{tap} Y[o(y,x,tap), (c,tap)] - x[c,y,x] * sum_{tap} Y[o(y,x,tap), SG])
+// over the taps whose output pixel o exists (col2im).  For C input channels
+// the implicit GEMM of pc2d_tc_bwd.cu runs its channel dimension as an MMA N
+// of 16 per block; this form puts C*T + 1 window columns there instead.
+//
+// GEMM kernel roles (320 threads, one CTA per SM, persistent over tiles):
+//   - warps 0-3, producers (one TMEM lane = one output pixel): per 32-K
+//     stage load g and hsum of 16 output channels at their pixel (coalesced
+//     across the warp; the next stage's rows are prefetched into L2), form
+//     g*hsum and g, split into tf32 hi + lo and tcgen05.st them (A operand);
+//   - warps 4-7, epilogue: drain the tile's accumulator (one of two TMEM
+//     slots) and write Y[n][col][o] (coalesced across pixels);
+//   - warp 8, MMA: one elected lane issues Ahi*Bhi + Alo*Bhi + Ahi*Blo
+//     (N = NP) per 8-wide K step, straight-line;
+//   - warp 9, loader: per stage one bulk copy of the pre-split weights.
+// Every wait is bounded; on a timeout the kernel records the error, stops,
+// drains its copies and MMAs and frees TMEM.
+#include <algorithm>
+#include <mutex>
+
+#include "pc2d_tc.cuh"
+#include "pc2d_tc_common.cuh"
+
+namespace pc2d {
+
+namespace {
+using namespace sm100;
+using tc::kWaitNs;
+using tc::warp_wait;
+
+constexpr int kTileM = 128;
+constexpr int kKS = 32;
+constexpr int kStages = 2;        // A stages in TMEM
+constexpr int kSlots = 2;         // accumulator slots
+constexpr int kMaxNP = 192;       // GEMM N (window columns + SG, multiple of 16)
+constexpr uint32_t kColSlot = 192;  // slot s at s * 192
+constexpr uint32_t kColA = 384;     // A stage st at 384 + 64 * st
+constexpr int kThreads = 320;
+constexpr int kMinSmem = 120 * 1024;
+constexpr int kSmemLimit = 227 * 1024;
+
+struct DcCfg {
+  int NY;           // Y columns: C*T + 1 (the last one is SG)
+  int NP;           // GEMM N: NY rounded up to 16
+  int nK;           // 32-K stages: K = 2m rounded up to 32
+  int tpi;          // 128-pixel tiles per image
+  int64_t tiles;    // n * tpi
+  uint32_t bstage;  // bytes of one stage's B: [hi: NP rows][lo: NP rows] x 128 B
+};
+
+DcCfg dc_cfg(const Problem &p) {
+  DcCfg c;
+  c.NY = p.C * p.T + 1;
+  c.NP = (c.NY + 15) / 16 * 16;
+  c.nK = ceil_div(2 * p.m, kKS);
+  c.tpi = (int)((p.PQ + kTileM - 1) / kTileM);
+  c.tiles = (int64_t)p.n * c.tpi;
+  c.bstage = (uint32_t)(2 * c.NP * 128);
+  return c;
+}
+
+inline size_t dc_bsplit_bytes(const DcCfg &c) { return (size_t)c.nK * c.bstage; }
+inline size_t dc_y_bytes(const Problem &p, const DcCfg &c) { return (size_t)p.n * c.NY * p.PQ * sizeof(float); }
+inline size_t dc_smem_bytes(const DcCfg &c) {
+  const size_t s = 1024 + (size_t)kStages * c.bstage + 16 * 8 + 64;
+  return std::max<size_t>(s, kMinSmem);
+}
+
+// B (weights) in the swizzled K-major layout the MMA reads: block kq =
+// [hi: NP rows][lo: NP rows], row n = window column, 32 K per row with 16-byte
+// chunk c stored at c ^ (n % 8).  K element k = 2j + w: w = 0 multiplies
+// g*hsum (h[j][n]), w = 1 multiplies g (p[j][n]; 1 in the SG column).
+// Grid (nK, NP / 16).
+__global__ void __launch_bounds__(256) tc_dc_prep_weights(const float *__restrict__ pars, Problem p, DcCfg c,
+                                                          float *__restrict__ wsB) {
+  const int kq = blockIdx.x;
+  float *blk = wsB + (int64_t)kq * 2 * c.NP * 32;
+  const float *h = pars + p.m;
+  const float *pp = h + (int64_t)p.m * p.d;
+  for (int e = threadIdx.x; e < 16 * 32; e += blockDim.x) {
+    const int n = blockIdx.y * 16 + e / 32, kk = e % 32;
+    const int k = kq * kKS + kk, j = k / 2, w = k & 1;
+    float v = 0.f;
+    if (j < p.m) {
+      if (n < c.NY - 1) v = (w == 0 ? h : pp)[(int64_t)j * p.d + n];
+      else if (n == c.NY - 1) v = w == 1 ? 1.f : 0.f;
+    }
+    const float hi = __uint_as_float(tf32_hi_bits(v));
+    const int pos = n * 32 + (((kk >> 2) ^ (n & 7)) << 2) + (kk & 3);
+    blk[pos] = hi;
+    blk[c.NP * 32 + pos] = v - hi;
+  }
+}
+
+template <int NP>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum, const float *__restrict__ wsB,
+                  Problem p, DcCfg c, float *__restrict__ Y, int *status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint8_t *sB = base;  // kStages x bstage
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + (size_t)kStages * c.bstage);
+  uint64_t *a_full = bars, *s_empty = bars + 2, *d_full = bars + 4, *d_empty = bars + 6, *final_bar = bars + 8;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 9);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      // 128 producer arrivals + the loader's arrival with the bytes of its copy
+      mbar_init(&a_full[i], 129);
+      mbar_init(&s_empty[i], 1);
+    }
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&d_full[i], 1);
+      mbar_init(&d_empty[i], 128);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  bool ok = true;
+
+  if (warp < 4) {
+    // ---------------------------------------------------------- producers
+    const int r = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    uint32_t it = 0;
+    for (int64_t t = blockIdx.x; t < c.tiles && ok; t += gridDim.x) {
+      const int64_t n = t / c.tpi;
+      const int o = (int)(t - n * c.tpi) * kTileM + r;
+      const bool valid = o < p.PQ;
+      const float *g0 = grad + n * p.m * p.PQ + o;
+      const float *h0 = hsum + n * p.m * p.PQ + o;
+      for (int kq = 0; kq < c.nK; ++kq, ++it) {
+        // next stage's rows of this pixel into L2
+        if (valid && kq + 1 < c.nK) {
+#pragma unroll
+          for (int jl = 0; jl < kKS / 2; ++jl) {
+            const int j = (kq + 1) * (kKS / 2) + jl;
+            if (j < p.m) {
+              prefetch_l2(g0 + (int64_t)j * p.PQ);
+              prefetch_l2(h0 + (int64_t)j * p.PQ);
+            }
+          }
+        }
+        float gv[kKS / 2], hv[kKS / 2];
+#pragma unroll
+        for (int jl = 0; jl < kKS / 2; ++jl) {
+          const int j = kq * (kKS / 2) + jl;
+          const bool in = valid && j < p.m;
+          gv[jl] = in ? __ldg(g0 + (int64_t)j * p.PQ) : 0.f;
+          hv[jl] = in ? __ldg(h0 + (int64_t)j * p.PQ) : 0.f;
+        }
+        uint32_t hi[kKS], lo[kKS];
+#pragma unroll
+        for (int jl = 0; jl < kKS / 2; ++jl) {
+          const float a0 = gv[jl] * hv[jl], a1 = gv[jl];
+          hi[2 * jl] = tf32_hi_bits(a0);
+          lo[2 * jl] = __float_as_uint(a0 - __uint_as_float(hi[2 * jl]));
+          hi[2 * jl + 1] = tf32_hi_bits(a1);
+          lo[2 * jl + 1] = __float_as_uint(a1 - __uint_as_float(hi[2 * jl + 1]));
+        }
+        // the MMAs that read this A stage last have completed
+        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acol = tmem + lane_off + kColA + st * 64;
+        tmem_st16(acol, *reinterpret_cast<const uint32_t(*)[16]>(&hi[0]));
+        tmem_st16(acol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&hi[16]));
+        tmem_st16(acol + 32, *reinterpret_cast<const uint32_t(*)[16]>(&lo[0]));
+        tmem_st16(acol + 48, *reinterpret_cast<const uint32_t(*)[16]>(&lo[16]));
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&a_full[st]);
+      }
+    }
+  } else if (warp < 8) {
+    // ---------------------------------------------------------- epilogue
+    const int qq = warp % 4;
+    const int r = qq * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(qq * 32) << 16;
+    uint32_t ti = 0;
+    for (int64_t t = blockIdx.x; t < c.tiles && ok; t += gridDim.x, ++ti) {
+      const uint32_t slot = ti % kSlots, ph = (ti / kSlots) & 1;
+      if (!warp_wait(&d_full[slot], ph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int64_t n = t / c.tpi;
+      const int o = (int)(t - n * c.tpi) * kTileM + r;
+      float *yb = Y + n * (int64_t)c.NY * p.PQ + o;
+      const uint32_t dcol = tmem + lane_off + slot * kColSlot;
+      // 32 columns per wait (16 for the last block of an odd multiple of 16)
+#pragma unroll
+      for (int cc = 0; cc < NP; cc += 32) {
+        uint32_t v[16], w[16];
+        if (cc + 16 < NP) {
+          tmem_ld16_nowait(dcol + cc, v);
+          tmem_ld16_nowait(dcol + cc + 16, w);
+          tmem_ld_wait_tie(v, w);
+        } else {
+          tmem_ld16_nowait(dcol + cc, v);
+          tmem_ld_wait_tie(v);
+        }
+        if (o < p.PQ) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            if (cc + q < c.NY) yb[(int64_t)(cc + q) * p.PQ] = __uint_as_float(v[q]);
+          if (cc + 16 < NP) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              if (cc + 16 + q < c.NY) yb[(int64_t)(cc + 16 + q) * p.PQ] = __uint_as_float(w[q]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&d_empty[slot]);
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------- MMA
+    const uint32_t idesc = idesc_tf32(kTileM, NP);
+    constexpr uint32_t kBlo = NP * 128;  // bytes of the hi rows of a stage
+    const uint32_t sB_addr = smem_u32(sB);
+    uint32_t it = 0, ti = 0;
+    for (int64_t t = blockIdx.x; t < c.tiles && ok; t += gridDim.x, ++ti) {
+      const uint32_t slot = ti % kSlots;
+      if (!warp_wait(&d_empty[slot], ((ti / kSlots) & 1) ^ 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const uint32_t dcol = tmem + slot * kColSlot;
+      for (int kq = 0; kq < c.nK; ++kq, ++it) {
+        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (!warp_wait(&a_full[st], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // straight-line issue from one elected lane, operands formed outside
+        const uint32_t ahi = tmem + kColA + st * 64, alo = ahi + 32;
+        const uint32_t bhi0 = sB_addr + st * c.bstage;
+        const uint32_t acc0 = kq == 0 ? 0u : 1u;
+        const bool last = kq == c.nK - 1;
+        if (elect_one()) {
+#pragma unroll
+          for (int ks = 0; ks < kKS / 8; ++ks) {
+            const uint32_t bhi = bhi0 + ks * 32, blo = bhi + kBlo;
+            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(bhi), idesc, ks == 0 ? acc0 : 1u);
+            mma_tf32_ts(dcol, alo + ks * 8, sdesc_kmajor_sw128(bhi), idesc, 1u);
+            mma_tf32_ts(dcol, ahi + ks * 8, sdesc_kmajor_sw128(blo), idesc, 1u);
+          }
+          tc_commit(&s_empty[st]);
+          if (last) tc_commit(&d_full[slot]);
+        }
+        __syncwarp();
+      }
+    }
+    if (elect_one()) tc_commit(final_bar);
+    __syncwarp();
+    mbar_wait(final_bar, 0, kWaitNs, nullptr);
+  } else {
+    // ------------------------------------------------------------- loader
+    uint32_t it = 0;
+    for (int64_t t = blockIdx.x; t < c.tiles && ok; t += gridDim.x) {
+      for (int kq = 0; kq < c.nK; ++kq, ++it) {
+        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&a_full[st], c.bstage);
+          bulk_g2s(sB + (size_t)st * c.bstage, wsB + (int64_t)kq * 2 * c.NP * 32, c.bstage, &a_full[st]);
+        }
+        __syncwarp();
+      }
+    }
+    // Drain: the copies issued last have landed before the CTA exits (the
+    // phase also needs the producers' arrivals, which come on every path
+    // that issued the copies without an abort).
+    const uint32_t last = it < (uint32_t)kStages ? it : (uint32_t)kStages;
+    for (uint32_t i = 0; i < last; ++i) {
+      const uint32_t idx = it - 1 - i;
+      mbar_wait(&a_full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
+    }
+  }
+
+  if (!ok) {
+    if (lane == 0) record_device_error(status, PC2D_ERR_TIMEOUT);
+    *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// col2im over stride phases: block (bx, n * s0 * s1 + ph) handles input
+// pixels (y, x) = (py + s0*a, px + s1*b) of phase ph = (py, px), one thread per
+// phase-grid position (a, b), consecutive b across a warp.  Only the taps
+// whose row/column offsets have the residues (py, px) reach these pixels, from
+// output pixel (a - dy, b - dx) with the tap's offsets (k0-1-ix2)*dl0 =
+// py + s0*dy, (k1-1-iy2)*dl1 = px + s1*dx; the block lists them in shared
+// memory in tap order (so the sums are deterministic) and every tap's loads
+// of Y are 32 consecutive output pixels per warp.
+//   dx = 2 * (sum_tap Y[o, (c,tap)] - x * sum_tap Y[o, SG]).
+constexpr int kColThreads = 256;
+constexpr int kMaxT = 256;
+__global__ void __launch_bounds__(kColThreads) tc_dc_col2im(const float *__restrict__ Y, const float *__restrict__ x,
+                                                            Problem p, DcCfg c, float *__restrict__ dx) {
+  __shared__ int s_tap[kMaxT], s_dy[kMaxT], s_dx[kMaxT];
+  __shared__ int s_wcnt[kColThreads / 32];
+  const int nph = p.s0 * p.s1;
+  const int64_t n = blockIdx.y / nph;
+  const int ph = (int)(blockIdx.y - n * nph);
+  const int py = ph / p.s1, px = ph - py * p.s1;
+  const int rows = p.H > py ? (p.H - py + p.s0 - 1) / p.s0 : 0;
+  const int cols = p.W > px ? (p.W - px + p.s1 - 1) / p.s1 : 0;
+  // this phase's taps, in tap order: ballot compaction per warp of 32 taps
+  int ntaps = 0;
+  for (int t0 = 0; t0 < p.T; t0 += kColThreads) {
+    const int t = t0 + (int)threadIdx.x;
+    bool v = false;
+    int dy = 0, dxo = 0;
+    if (t < p.T) {
+      const int rr = tap_row(p, t), cc = tap_col(p, t);
+      v = (rr % p.s0) == py && (cc % p.s1) == px;
+      dy = (rr - py) / p.s0;
+      dxo = (cc - px) / p.s1;
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, v);
+    const int lane = threadIdx.x % 32, w = threadIdx.x / 32;
+    if (lane == 0) s_wcnt[w] = __popc(bal);
+    __syncthreads();
+    int base = ntaps;
+    for (int i = 0; i < w; ++i) base += s_wcnt[i];
+    if (v) {
+      const int pos = base + __popc(bal & ((1u << lane) - 1u));
+      s_tap[pos] = t;
+      s_dy[pos] = dy;
+      s_dx[pos] = dxo;
+    }
+    for (int i = 0; i < kColThreads / 32; ++i) ntaps += s_wcnt[i];
+    __syncthreads();
+  }
+  const int64_t q = (int64_t)blockIdx.x * kColThreads + threadIdx.x;
+  if (q >= (int64_t)rows * cols) return;
+  const int a = (int)(q / cols), b = (int)(q - (int64_t)(q / cols) * cols);
+  const float *yb = Y + n * (int64_t)c.NY * p.PQ;
+  float acc[8];
+#pragma unroll
+  for (int ci = 0; ci < 8; ++ci) acc[ci] = 0.f;
+  float sg = 0.f;
+  for (int i = 0; i < ntaps; ++i) {
+    const int oy = a - s_dy[i], ox = b - s_dx[i];
+    if (oy < 0 || ox < 0 || oy >= p.P || ox >= p.Q) continue;
+    const int64_t o = (int64_t)oy * p.Q + ox;
+    const int tap = s_tap[i];
+    sg += __ldg(yb + (int64_t)(c.NY - 1) * p.PQ + o);
+#pragma unroll
+    for (int ci = 0; ci < 8; ++ci)
+      if (ci < p.C) acc[ci] += __ldg(yb + (int64_t)(ci * p.T + tap) * p.PQ + o);
+  }
+  const int y = py + p.s0 * a, xc = px + p.s1 * b;
+#pragma unroll
+  for (int ci = 0; ci < 8; ++ci) {
+    if (ci < p.C) {
+      const int64_t xi = n * p.CHW + (int64_t)ci * p.HW + (int64_t)y * p.W + xc;
+      dx[xi] = 2.f * (acc[ci] - __ldg(x + xi) * sg);
+    }
+  }
+}
+
+std::mutex g_attr_mutex;
+bool g_attr_set[64][kMaxNP / 16] = {};
+
+template <int NP>
+int launch_dc_gemm(const Problem &p, const DcCfg &c, const float *grad, const float *hsum, const float *wsB, float *Y,
+                   int *status, cudaStream_t stream) {
+  int dev = 0;
+  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (dev >= 0 && dev < 64 && !g_attr_set[dev][NP / 16 - 1]) {
+      PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_dc_gemm_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kSmemLimit));
+      g_attr_set[dev][NP / 16 - 1] = true;
+    }
+  }
+  const int grid = (int)std::min<int64_t>(c.tiles, device_sm_count());
+  tc_dc_gemm_kernel<NP><<<grid, kThreads, dc_smem_bytes(c), stream>>>(grad, hsum, wsB, p, c, Y, status);
+  PC2D_LAUNCH_CHECK("tc_dc_gemm_kernel");
+  return PC2D_OK;
+}
+
+}  // namespace
+
+bool tc_dgcol_supported(const Problem &p) {
+  // at least one 128-pixel tile per SM: below that the three launches of this
+  // path cost more than the implicit GEMM's one
+  if (p.NPQ < (int64_t)148 * kTileM || p.m < 1 || p.C > 8 || p.HW >= ((int64_t)1 << 30) ||
+      p.PQ >= ((int64_t)1 << 30))
+    return false;
+  const DcCfg c = dc_cfg(p);
+  return c.NP <= kMaxNP && p.T <= kMaxT && (int64_t)p.n * p.s0 * p.s1 < 65536 && dc_smem_bytes(c) <= (size_t)kSmemLimit;
+}
+
+size_t tc_dgcol_workspace(const Problem &p) {
+  const DcCfg c = dc_cfg(p);
+  return align_up(dc_bsplit_bytes(c), 256) + align_up(dc_y_bytes(p, c), 256);
+}
+
+int tc_dgcol(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, float *dx,
+             void *ws, cudaStream_t stream) {
+  const DcCfg c = dc_cfg(p);
+  int *status = device_status_ptr();
+  if (!status) {
+    set_last_error("could not resolve the device status word");
+    return PC2D_ERR_CUDA;
+  }
+  float *wsB = reinterpret_cast<float *>(ws);
+  float *Y = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + align_up(dc_bsplit_bytes(c), 256));
+  timing_begin(K_DGRAD, stream);
+  tc_dc_prep_weights<<<dim3(c.nK, c.NP / 16), 256, 0, stream>>>(pars, p, c, wsB);
+  PC2D_LAUNCH_CHECK("tc_dc_prep_weights");
+  int st = PC2D_OK;
+  switch (c.NP / 16) {
+#define PC2D_DC_CASE(k) \
+  case k: st = launch_dc_gemm<16 * k>(p, c, grad, hsum, wsB, Y, status, stream); break;
+    PC2D_DC_CASE(1) PC2D_DC_CASE(2) PC2D_DC_CASE(3) PC2D_DC_CASE(4) PC2D_DC_CASE(5) PC2D_DC_CASE(6)
+    PC2D_DC_CASE(7) PC2D_DC_CASE(8) PC2D_DC_CASE(9) PC2D_DC_CASE(10) PC2D_DC_CASE(11) PC2D_DC_CASE(12)
+#undef PC2D_DC_CASE
+    default:
+      set_last_error("internal: unsupported GEMM width %d", c.NP);
+      return PC2D_ERR_UNSUPPORTED;
+  }
+  if (st != PC2D_OK) return st;
+  {
+    // phase grids: at most ceil(H/s0) x ceil(W/s1) pixels each
+    const int64_t ppg = (int64_t)((p.H + p.s0 - 1) / p.s0) * ((p.W + p.s1 - 1) / p.s1);
+    const dim3 cgrid((unsigned)((ppg + kColThreads - 1) / kColThreads), (unsigned)(p.n * p.s0 * p.s1));
+    tc_dc_col2im<<<cgrid, kColThreads, 0, stream>>>(Y, x, p, c, dx);
+  }
+  PC2D_LAUNCH_CHECK("tc_dc_col2im");
+  timing_end(K_DGRAD, stream);
+  return PC2D_OK;
+}
+
+}  // namespace pc2d

@@ -117,6 +117,8 @@ MEDIUM = {
     "c40_m48_k3x5_s2x1_dl1x2_odd": dict(n=3, C=40, H=23, W=23, m=48, k=(3, 5), s=(2, 1), dl=(1, 2)),
     "c64_m32_k3_aligned": dict(n=2, C=64, H=18, W=18, m=32, k=(3, 3), s=(1, 1), dl=(1, 1)),
     "c48_m80_k3_s2": dict(n=2, C=48, H=21, W=21, m=80, k=(3, 3), s=(2, 2), dl=(1, 1)),
+    # few input channels: the output-pixel GEMM + col2im input gradient
+    "c5_m24_k5x3_s1x2_dl2x1_narrow": dict(n=16, C=5, H=60, W=60, m=24, k=(5, 3), s=(1, 2), dl=(2, 1)),
 }
 
 
@@ -142,6 +144,21 @@ def test_medium_shapes_vs_float64(name):
     ref_out, ref_hs, rdx, rdp = torch_reference(xd, pd, 1.0, k, s, dl, grad=g.cuda())
     check_outputs(out.cpu().numpy(), hsum.cpu().numpy(), ref_out, ref_hs)
     check_grads(dx.cpu().numpy(), dp.cpu().numpy(), rdx, rdp, m, d)
+
+
+def test_full_size_backward_c4_vs_float64():
+    """Full-size c4 backward (3 input channels: the output-pixel GEMM + col2im
+    input gradient, k7 stride 2) against the float64 torch restatement."""
+    wl = workloads.WORKLOADS["c4"]
+    L = wl.layer
+    x, pars, g = workloads.draw(wl)
+    grad = workloads.draw_grad(wl, g).cuda()
+    xp = workloads.pad_input(x, L.p).cuda()
+    p = pars[0].cuda()
+    out, hsum = forward(xp, p, 1.0, L.k, L.s, 1)
+    dx, dp = backward(grad, xp, p, hsum, 1.0, L.k, L.s, 1)
+    _, _, rdx, rdp = torch_reference(xp, p, 1.0, (L.k, L.k), L.s, 1, grad=grad)
+    check_grads(dx.cpu().numpy(), dp.cpu().numpy(), rdx, rdp, L.cout, L.cin * L.k * L.k)
 
 
 @pytest.mark.parametrize("algo_name", sorted(ALGOS))
