@@ -18,17 +18,20 @@
 //
 // GEMM kernel roles (320 threads, one CTA per SM, persistent over tiles):
 //   - warps 0-3, producers (one TMEM lane = one output pixel): per 32-K
-//     stage load g and hsum of 16 output channels at their pixel (coalesced
-//     across the warp; the next stage's rows are prefetched into L2), form
-//     g*hsum and g, split into tf32 hi + lo and tcgen05.st them (A operand);
+//     stage read g and hsum of 16 output channels at their pixel (from the
+//     [16 x 128] tiles the loader staged, or straight from global memory
+//     with an L2 prefetch of the next stage), form g*hsum and g, split into
+//     tf32 hi + lo and tcgen05.st them (A operand);
 //   - warps 4-7, epilogue: drain the tile's accumulator (one of two TMEM
 //     slots) and write Y[n][col][o] (coalesced across pixels);
 //   - warp 8, MMA: one elected lane issues Ahi*Bhi + Alo*Bhi + Ahi*Blo
 //     (N = NP) per 8-wide K step, straight-line;
-//   - warp 9, loader: per stage one bulk copy of the pre-split weights.
+//   - warp 9, loader: per stage the g and hsum tiles (two 2-D tensor copies)
+//     and one bulk copy of the pre-split weights.
 // Every wait is bounded; on a timeout the kernel records the error, stops,
 // drains its copies and MMAs and frees TMEM.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "pc2d_tc.cuh"
@@ -59,6 +62,7 @@ struct DcCfg {
   int tpi;          // 128-pixel tiles per image
   int64_t tiles;    // n * tpi
   uint32_t bstage;  // bytes of one stage's B: [hi: NP rows][lo: NP rows] x 128 B
+  int tma;          // 1: a stage's g and hsum tiles [16 channels][128 pixels] are 2-D tensor copies
 };
 
 DcCfg dc_cfg(const Problem &p) {
@@ -69,13 +73,15 @@ DcCfg dc_cfg(const Problem &p) {
   c.tpi = (int)((p.PQ + kTileM - 1) / kTileM);
   c.tiles = (int64_t)p.n * c.tpi;
   c.bstage = (uint32_t)(2 * c.NP * 128);
+  c.tma = (p.PQ % 4 == 0 && (int64_t)p.n * p.m < ((int64_t)1 << 31)) ? 1 : 0;
   return c;
 }
 
 inline size_t dc_bsplit_bytes(const DcCfg &c) { return (size_t)c.nK * c.bstage; }
 inline size_t dc_y_bytes(const Problem &p, const DcCfg &c) { return (size_t)p.n * c.NY * p.PQ * sizeof(float); }
+constexpr uint32_t kTileBytes = 16 * kTileM * 4;  // one [16 channels][128 pixels] tile
 inline size_t dc_smem_bytes(const DcCfg &c) {
-  const size_t s = 1024 + (size_t)kStages * c.bstage + 16 * 8 + 64;
+  const size_t s = 1024 + (size_t)kStages * (c.bstage + 2 * kTileBytes) + 16 * 8 + 64;
   return std::max<size_t>(s, kMinSmem);
 }
 
@@ -108,14 +114,17 @@ __global__ void __launch_bounds__(256) tc_dc_prep_weights(const float *__restric
 template <int NP>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum, const float *__restrict__ wsB,
-                  Problem p, DcCfg c, float *__restrict__ Y, int *status) {
+                  Problem p, DcCfg c, const __grid_constant__ CUtensorMap gmap,
+                  const __grid_constant__ CUtensorMap hmap, float *__restrict__ Y, int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  uint8_t *sB = base;  // kStages x bstage
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + (size_t)kStages * c.bstage);
+  uint8_t *sB = base;                                          // kStages x bstage
+  float *sT = reinterpret_cast<float *>(sB + (size_t)kStages * c.bstage);  // kStages x [g tile | hsum tile]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sT + kStages * 2 * 16 * kTileM);
   uint64_t *a_full = bars, *s_empty = bars + 2, *d_full = bars + 4, *d_empty = bars + 6, *final_bar = bars + 8;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 9);
+  uint64_t *t_full = bars + 9, *t_empty = bars + 11;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 13);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   if (threadIdx.x == 0) {
@@ -127,6 +136,10 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&d_full[i], 1);
       mbar_init(&d_empty[i], 128);
+    }
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&t_full[i], 1);
+      mbar_init(&t_empty[i], 128);
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
@@ -154,24 +167,40 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
       const float *g0 = grad + n * p.m * p.PQ + o;
       const float *h0 = hsum + n * p.m * p.PQ + o;
       for (int kq = 0; kq < c.nK; ++kq, ++it) {
-        // next stage's rows of this pixel into L2
-        if (valid && kq + 1 < c.nK) {
+        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        float gv[kKS / 2], hv[kKS / 2];
+        if (c.tma) {
+          if (!warp_wait(&t_full[st], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const float *tg = sT + st * 2 * 16 * kTileM;
 #pragma unroll
           for (int jl = 0; jl < kKS / 2; ++jl) {
-            const int j = (kq + 1) * (kKS / 2) + jl;
-            if (j < p.m) {
-              prefetch_l2(g0 + (int64_t)j * p.PQ);
-              prefetch_l2(h0 + (int64_t)j * p.PQ);
+            const bool in = valid && kq * (kKS / 2) + jl < p.m;
+            gv[jl] = in ? tg[jl * kTileM + r] : 0.f;
+            hv[jl] = in ? tg[(16 + jl) * kTileM + r] : 0.f;
+          }
+          mbar_arrive(&t_empty[st]);
+        } else {
+          // next stage's rows of this pixel into L2
+          if (valid && kq + 1 < c.nK) {
+#pragma unroll
+            for (int jl = 0; jl < kKS / 2; ++jl) {
+              const int j = (kq + 1) * (kKS / 2) + jl;
+              if (j < p.m) {
+                prefetch_l2(g0 + (int64_t)j * p.PQ);
+                prefetch_l2(h0 + (int64_t)j * p.PQ);
+              }
             }
           }
-        }
-        float gv[kKS / 2], hv[kKS / 2];
 #pragma unroll
-        for (int jl = 0; jl < kKS / 2; ++jl) {
-          const int j = kq * (kKS / 2) + jl;
-          const bool in = valid && j < p.m;
-          gv[jl] = in ? __ldg(g0 + (int64_t)j * p.PQ) : 0.f;
-          hv[jl] = in ? __ldg(h0 + (int64_t)j * p.PQ) : 0.f;
+          for (int jl = 0; jl < kKS / 2; ++jl) {
+            const int j = kq * (kKS / 2) + jl;
+            const bool in = valid && j < p.m;
+            gv[jl] = in ? __ldg(g0 + (int64_t)j * p.PQ) : 0.f;
+            hv[jl] = in ? __ldg(h0 + (int64_t)j * p.PQ) : 0.f;
+          }
         }
         uint32_t hi[kKS], lo[kKS];
 #pragma unroll
@@ -183,7 +212,6 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
           lo[2 * jl + 1] = __float_as_uint(a1 - __uint_as_float(hi[2 * jl + 1]));
         }
         // the MMAs that read this A stage last have completed
-        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
         if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
           ok = false;
           break;
@@ -288,8 +316,26 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
     // ------------------------------------------------------------- loader
     uint32_t it = 0;
     for (int64_t t = blockIdx.x; t < c.tiles && ok; t += gridDim.x) {
+      const int64_t n = t / c.tpi;
+      const int o0 = (int)(t - n * c.tpi) * kTileM;
       for (int kq = 0; kq < c.nK; ++kq, ++it) {
         const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        if (c.tma) {
+          // g and hsum of channels kq*16 .. +15 at the tile's pixels (channels
+          // past m are never read; pixels past the image are zero)
+          if (!warp_wait(&t_empty[st], ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            float *tg = sT + st * 2 * 16 * kTileM;
+            const int yc = (int)(n * p.m + kq * (kKS / 2));
+            mbar_arrive_expect_tx(&t_full[st], 2 * kTileBytes);
+            tma_load_2d(tg, &gmap, o0, yc, &t_full[st]);
+            tma_load_2d(tg + 16 * kTileM, &hmap, o0, yc, &t_full[st]);
+          }
+          __syncwarp();
+        }
         if (!warp_wait(&s_empty[st], ph ^ 1, abort_flag)) {
           ok = false;
           break;
@@ -299,6 +345,13 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
           bulk_g2s(sB + (size_t)st * c.bstage, wsB + (int64_t)kq * 2 * c.NP * 32, c.bstage, &a_full[st]);
         }
         __syncwarp();
+      }
+    }
+    if (c.tma) {
+      const uint32_t tl = it < (uint32_t)kStages ? it : (uint32_t)kStages;
+      for (uint32_t i = 0; i < tl; ++i) {
+        const uint32_t idx = it - 1 - i;
+        mbar_wait(&t_full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
       }
     }
     // Drain: the copies issued last have landed before the CTA exits (the
@@ -379,15 +432,32 @@ __global__ void __launch_bounds__(kColThreads) tc_dc_col2im(const float *__restr
 #pragma unroll
   for (int ci = 0; ci < 8; ++ci) acc[ci] = 0.f;
   float sg = 0.f;
-  for (int i = 0; i < ntaps; ++i) {
-    const int oy = a - s_dy[i], ox = b - s_dx[i];
-    if (oy < 0 || ox < 0 || oy >= p.P || ox >= p.Q) continue;
-    const int64_t o = (int64_t)oy * p.Q + ox;
-    const int tap = s_tap[i];
-    sg += __ldg(yb + (int64_t)(c.NY - 1) * p.PQ + o);
+  // groups of 4 taps: all loads of a group first (latency overlap), then the
+  // adds in tap order
+  for (int i0 = 0; i0 < ntaps; i0 += 4) {
+    float ys[4], yv[4][8];
 #pragma unroll
-    for (int ci = 0; ci < 8; ++ci)
-      if (ci < p.C) acc[ci] += __ldg(yb + (int64_t)(ci * p.T + tap) * p.PQ + o);
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u;
+      bool v = i < ntaps;
+      int64_t o = 0;
+      int tap = 0;
+      if (v) {
+        const int oy = a - s_dy[i], ox = b - s_dx[i];
+        v = oy >= 0 && ox >= 0 && oy < p.P && ox < p.Q;
+        o = (int64_t)oy * p.Q + ox;
+        tap = s_tap[i];
+      }
+      ys[u] = v ? __ldg(yb + (int64_t)(c.NY - 1) * p.PQ + o) : 0.f;
+#pragma unroll
+      for (int ci = 0; ci < 8; ++ci) yv[u][ci] = (v && ci < p.C) ? __ldg(yb + (int64_t)(ci * p.T + tap) * p.PQ + o) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      sg += ys[u];
+#pragma unroll
+      for (int ci = 0; ci < 8; ++ci) acc[ci] += yv[u][ci];
+    }
   }
   const int y = py + p.s0 * a, xc = px + p.s1 * b;
 #pragma unroll
@@ -403,8 +473,15 @@ std::mutex g_attr_mutex;
 bool g_attr_set[64][kMaxNP / 16] = {};
 
 template <int NP>
-int launch_dc_gemm(const Problem &p, const DcCfg &c, const float *grad, const float *hsum, const float *wsB, float *Y,
+int launch_dc_gemm(const Problem &p, DcCfg c, const float *grad, const float *hsum, const float *wsB, float *Y,
                    int *status, cudaStream_t stream) {
+  // g and hsum viewed as [n*m rows][PQ floats], boxes of 16 rows x 128 floats
+  CUtensorMap gmap, hmap;
+  std::memset(&gmap, 0, sizeof(gmap));
+  std::memset(&hmap, 0, sizeof(hmap));
+  if (c.tma && !(encode_planes_map(grad, p.PQ, (int64_t)p.n * p.m, kTileM, 16, &gmap) &&
+                 encode_planes_map(hsum, p.PQ, (int64_t)p.n * p.m, kTileM, 16, &hmap)))
+    c.tma = 0;  // direct global loads instead
   int dev = 0;
   PC2D_CUDA_CHECK(cudaGetDevice(&dev));
   {
@@ -416,7 +493,7 @@ int launch_dc_gemm(const Problem &p, const DcCfg &c, const float *grad, const fl
     }
   }
   const int grid = (int)std::min<int64_t>(c.tiles, device_sm_count());
-  tc_dc_gemm_kernel<NP><<<grid, kThreads, dc_smem_bytes(c), stream>>>(grad, hsum, wsB, p, c, Y, status);
+  tc_dc_gemm_kernel<NP><<<grid, kThreads, dc_smem_bytes(c), stream>>>(grad, hsum, wsB, p, c, gmap, hmap, Y, status);
   PC2D_LAUNCH_CHECK("tc_dc_gemm_kernel");
   return PC2D_OK;
 }
