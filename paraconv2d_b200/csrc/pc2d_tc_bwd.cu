@@ -323,6 +323,9 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   bool ok = true;
+  // The parameter-gradient kernel launched after this one reads nothing it
+  // writes: let it start on SMs this grid has left.
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp < 4) {
     // ---------------------------------------------------------- producers

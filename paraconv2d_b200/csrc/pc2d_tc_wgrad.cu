@@ -680,7 +680,24 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   }
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
   timing_begin(K_WGRAD, stream);
-  tc_wgrad_kernel<<<grid, kThreads, wg_smem_bytes(c), stream>>>(grad, x, hsum, p, c, xmap, part, sums, status);
+  // Programmatic dependent launch: when the input-gradient kernel precedes
+  // this one on the stream, this grid may start on the SMs it has left (it
+  // reads none of that kernel's outputs, and their workspace regions are
+  // disjoint; everything earlier on the stream has completed before that
+  // kernel's own launch).  After any other kernel it starts as usual.
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = wg_smem_bytes(c);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tc_wgrad_kernel, grad, x, hsum, p, c, xmap, part, sums, status));
+  }
   timing_end(K_WGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
   const dim3 fgrid(ceil_div(p.d, kFinK), p.m);
