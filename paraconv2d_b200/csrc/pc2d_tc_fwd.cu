@@ -128,7 +128,7 @@ FwdCfg fwd_cfg(const Problem &p) {
 inline size_t fwd_bsplit_bytes(const FwdCfg &c) { return (size_t)c.ncb * c.nKB * c.bstage; }
 inline size_t fwd_smem_bytes(const Problem &p, const FwdCfg &c) {
   size_t s = 1024 + (size_t)c.nst * c.sstage + (size_t)c.nKB * kKS * 8 + (size_t)kMaxStages * kKS * 4 +
-             (size_t)kMaxStages * kMaxCh * 4 + 2 * kTileM * 4 + 24 * 8 + 64;
+             (size_t)kMaxStages * kMaxCh * 4 + 2 * kTileM * 4 + 4 * 2 * 64 * 4 + 24 * 8 + 64;
   (void)p;
   return std::max<size_t>(s, kMinSmem);
 }
@@ -217,6 +217,7 @@ struct Smem {
   int *offs;        // [stage][32 SUB] halo offset of each K of the stage (-1 = zero)
   int *lead;        // [stage][64] floats before each halo plane's first element
   float *s2buf;     // [tile buffer 2][128]
+  float *hcbuf;     // [epilogue warp 4][h0 64 | cj 64] of the item's channel block
   uint64_t *full, *a_full, *s_empty, *gr_full, *gr_empty, *s2_full, *s2_empty, *final_bar;
   uint32_t *tmem_holder;
   volatile int *abort_flag;
@@ -239,8 +240,9 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   S.offs = reinterpret_cast<int *>(S.koff + c.nK * kKStage);
   S.lead = S.offs + kMaxStages * kKS;
   S.s2buf = reinterpret_cast<float *>(S.lead + kMaxStages * kMaxCh);
+  S.hcbuf = S.s2buf + 2 * kTileM;
   uint64_t *bars = reinterpret_cast<uint64_t *>(
-      (reinterpret_cast<uintptr_t>(S.s2buf + 2 * kTileM) + 7) & ~(uintptr_t)7);
+      (reinterpret_cast<uintptr_t>(S.hcbuf + 4 * 2 * 64) + 7) & ~(uintptr_t)7);
   S.full = bars;            // [4] halo + B + offsets landed (loader expect_tx)
   S.a_full = bars + 4;      // [4] A stage in TMEM (128 producer arrivals)
   S.s_empty = bars + 8;     // [4] stage consumed by the MMAs (commit)
@@ -422,15 +424,36 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
       const int pix = (int)(t - nimg * c.tpi) * kTileM + r;
       const bool valid = pix < p.PQ;
       const int64_t obase = nimg * (int64_t)p.m * p.PQ + pix;
+      // h0 and |P|^2 + p0^2 of the block's channels: this warp's copy in
+      // shared memory (two per lane), then all outputs in registers, then the
+      // stores
+      float *hc = S.hcbuf + q * 2 * 64;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int jj = lane + 32 * e;
+        if (jj < NB) {
+          const int j = cb * NB + jj;
+          hc[jj] = j < p.m ? __ldg(h0 + j) : 0.f;
+          hc[64 + jj] = __ldg(cj + cb * NB + jj);
+        }
+      }
+      __syncwarp();
 #pragma unroll
       for (int jj = 0; jj < NB; ++jj) {
-        const int j = cb * NB + jj;
-        if (valid && j < p.m) {
-          const float hs = __ldg(h0 + j) + hacc[jj];
-          const float o = factor * (fmaf(hs, hs, -s2) + 2.f * pacc[jj] - __ldg(cj + cb * NB + jj));
-          const int64_t oi = obase + (int64_t)j * p.PQ;
-          out[oi] = o;
-          hsum[oi] = hs;
+        const float hs = hc[jj] + hacc[jj];
+        pacc[jj] = factor * (fmaf(hs, hs, -s2) + 2.f * pacc[jj] - hc[64 + jj]);
+        hacc[jj] = hs;
+      }
+      __syncwarp();
+      if (valid) {
+#pragma unroll
+        for (int jj = 0; jj < NB; ++jj) {
+          const int j = cb * NB + jj;
+          if (j < p.m) {
+            const int64_t oi = obase + (int64_t)j * p.PQ;
+            out[oi] = pacc[jj];
+            hsum[oi] = hacc[jj];
+          }
         }
       }
     }
