@@ -31,6 +31,7 @@
 // Every wait is bounded; on a timeout the kernel records the error, stops,
 // drains its copies and MMAs and frees TMEM.
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <mutex>
 
@@ -385,18 +386,66 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
 // memory in tap order (so the sums are deterministic) and every tap's loads
 // of Y are 32 consecutive output pixels per warp.
 //   dx = 2 * (sum_tap Y[o, (c,tap)] - x * sum_tap Y[o, SG]).
+// Each listed tap carries its Y offset relative to the thread's own position
+// a*Q + b (tap*PQ - dy*Q - dx, and dy*Q + dx for the SG column), so a thread
+// whose taps all land inside the output (the interior of the phase grid)
+// loads without any per-tap arithmetic beyond one add; border threads check
+// each tap's output pixel.  An image's Y is below 2^31 floats.
 constexpr int kColThreads = 256;
 constexpr int kMaxT = 256;
+
+template <int CC, bool CHECK>
+__device__ __forceinline__ void col2im_taps(const float *__restrict__ yb, const float *__restrict__ ysg, int ntaps,
+                                            const int2 *s_tp, const int2 *s_d, int cstride, int a, int b, int P, int Q,
+                                            float (&acc)[CC], float &sg) {
+  // groups of 4 taps: all loads of a group first (latency overlap), then the
+  // adds in tap order
+  for (int i0 = 0; i0 < ntaps; i0 += 4) {
+    float ys[4], yv[4][CC];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u;
+      bool v = i < ntaps;
+      int2 tp = make_int2(0, 0);
+      if (v) {
+        tp = s_tp[i];
+        if (CHECK) {
+          const int2 d = s_d[i];
+          const int oy = a - d.x, ox = b - d.y;
+          v = oy >= 0 && ox >= 0 && oy < P && ox < Q;
+        }
+      }
+      ys[u] = v ? __ldg(ysg - tp.y) : 0.f;
+#pragma unroll
+      for (int ci = 0; ci < CC; ++ci) yv[u][ci] = v ? __ldg(yb + tp.x + ci * cstride) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (i0 + u < ntaps) {
+        sg += ys[u];
+#pragma unroll
+        for (int ci = 0; ci < CC; ++ci) acc[ci] += yv[u][ci];
+      }
+    }
+  }
+}
+
+template <int CC>
 __global__ void __launch_bounds__(kColThreads) tc_dc_col2im(const float *__restrict__ Y, const float *__restrict__ x,
                                                             Problem p, DcCfg c, float *__restrict__ dx) {
-  __shared__ int s_tap[kMaxT], s_dy[kMaxT], s_dx[kMaxT];
+  __shared__ int2 s_tp[kMaxT];  // (tap*PQ - (dy*Q + dx), dy*Q + dx) of the phase's taps, tap order
+  __shared__ int2 s_d[kMaxT];   // (dy, dx)
   __shared__ int s_wcnt[kColThreads / 32];
+  __shared__ int s_ext[4];      // max dy, max dx, -min dy, -min dx
   const int nph = p.s0 * p.s1;
   const int64_t n = blockIdx.y / nph;
   const int ph = (int)(blockIdx.y - n * nph);
   const int py = ph / p.s1, px = ph - py * p.s1;
   const int rows = p.H > py ? (p.H - py + p.s0 - 1) / p.s0 : 0;
   const int cols = p.W > px ? (p.W - px + p.s1 - 1) / p.s1 : 0;
+  const int PQ = (int)p.PQ, Q = p.Q;
+  if (threadIdx.x < 4) s_ext[threadIdx.x] = INT_MIN;
+  __syncthreads();
   // this phase's taps, in tap order: ballot compaction per warp of 32 taps
   int ntaps = 0;
   for (int t0 = 0; t0 < p.T; t0 += kColThreads) {
@@ -412,14 +461,20 @@ __global__ void __launch_bounds__(kColThreads) tc_dc_col2im(const float *__restr
     const unsigned bal = __ballot_sync(0xffffffffu, v);
     const int lane = threadIdx.x % 32, w = threadIdx.x / 32;
     if (lane == 0) s_wcnt[w] = __popc(bal);
+    if (v) {
+      atomicMax(&s_ext[0], dy);
+      atomicMax(&s_ext[1], dxo);
+      atomicMax(&s_ext[2], -dy);
+      atomicMax(&s_ext[3], -dxo);
+    }
     __syncthreads();
     int base = ntaps;
     for (int i = 0; i < w; ++i) base += s_wcnt[i];
     if (v) {
       const int pos = base + __popc(bal & ((1u << lane) - 1u));
-      s_tap[pos] = t;
-      s_dy[pos] = dy;
-      s_dx[pos] = dxo;
+      const int dd = dy * Q + dxo;
+      s_tp[pos] = make_int2(t * PQ - dd, dd);
+      s_d[pos] = make_int2(dy, dxo);
     }
     for (int i = 0; i < kColThreads / 32; ++i) ntaps += s_wcnt[i];
     __syncthreads();
@@ -427,45 +482,23 @@ __global__ void __launch_bounds__(kColThreads) tc_dc_col2im(const float *__restr
   const int64_t q = (int64_t)blockIdx.x * kColThreads + threadIdx.x;
   if (q >= (int64_t)rows * cols) return;
   const int a = (int)(q / cols), b = (int)(q - (int64_t)(q / cols) * cols);
-  const float *yb = Y + n * (int64_t)c.NY * p.PQ;
-  float acc[8];
+  const int own = a * Q + b;  // may exceed the output grid; only offsets from it are loaded
+  const float *yb = Y + n * (int64_t)c.NY * p.PQ + own;
+  const float *ysg = yb + (int64_t)(c.NY - 1) * p.PQ;
+  float acc[CC];
 #pragma unroll
-  for (int ci = 0; ci < 8; ++ci) acc[ci] = 0.f;
+  for (int ci = 0; ci < CC; ++ci) acc[ci] = 0.f;
   float sg = 0.f;
-  // groups of 4 taps: all loads of a group first (latency overlap), then the
-  // adds in tap order
-  for (int i0 = 0; i0 < ntaps; i0 += 4) {
-    float ys[4], yv[4][8];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u;
-      bool v = i < ntaps;
-      int64_t o = 0;
-      int tap = 0;
-      if (v) {
-        const int oy = a - s_dy[i], ox = b - s_dx[i];
-        v = oy >= 0 && ox >= 0 && oy < p.P && ox < p.Q;
-        o = (int64_t)oy * p.Q + ox;
-        tap = s_tap[i];
-      }
-      ys[u] = v ? __ldg(yb + (int64_t)(c.NY - 1) * p.PQ + o) : 0.f;
-#pragma unroll
-      for (int ci = 0; ci < 8; ++ci) yv[u][ci] = (v && ci < p.C) ? __ldg(yb + (int64_t)(ci * p.T + tap) * p.PQ + o) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      sg += ys[u];
-#pragma unroll
-      for (int ci = 0; ci < 8; ++ci) acc[ci] += yv[u][ci];
-    }
-  }
+  const bool interior = ntaps > 0 && a - s_ext[0] >= 0 && b - s_ext[1] >= 0 && a + s_ext[2] < p.P && b + s_ext[3] < Q;
+  if (interior)
+    col2im_taps<CC, false>(yb, ysg, ntaps, s_tp, s_d, p.T * PQ, a, b, p.P, Q, acc, sg);
+  else
+    col2im_taps<CC, true>(yb, ysg, ntaps, s_tp, s_d, p.T * PQ, a, b, p.P, Q, acc, sg);
   const int y = py + p.s0 * a, xc = px + p.s1 * b;
 #pragma unroll
-  for (int ci = 0; ci < 8; ++ci) {
-    if (ci < p.C) {
-      const int64_t xi = n * p.CHW + (int64_t)ci * p.HW + (int64_t)y * p.W + xc;
-      dx[xi] = 2.f * (acc[ci] - __ldg(x + xi) * sg);
-    }
+  for (int ci = 0; ci < CC; ++ci) {
+    const int64_t xi = n * p.CHW + (int64_t)ci * p.HW + (int64_t)y * p.W + xc;
+    dx[xi] = 2.f * (acc[ci] - __ldg(x + xi) * sg);
   }
 }
 
@@ -507,7 +540,8 @@ bool tc_dgcol_supported(const Problem &p) {
       p.PQ >= ((int64_t)1 << 30))
     return false;
   const DcCfg c = dc_cfg(p);
-  return c.NP <= kMaxNP && p.T <= kMaxT && (int64_t)p.n * p.s0 * p.s1 < 65536 && dc_smem_bytes(c) <= (size_t)kSmemLimit;
+  return c.NP <= kMaxNP && p.T <= kMaxT && (int64_t)p.n * p.s0 * p.s1 < 65536 && (int64_t)c.NY * p.PQ < ((int64_t)1 << 31) &&
+         dc_smem_bytes(c) <= (size_t)kSmemLimit;
 }
 
 size_t tc_dgcol_workspace(const Problem &p) {
@@ -544,7 +578,16 @@ int tc_dgcol(const Problem &p, const float *grad, const float *x, const float *p
     // phase grids: at most ceil(H/s0) x ceil(W/s1) pixels each
     const int64_t ppg = (int64_t)((p.H + p.s0 - 1) / p.s0) * ((p.W + p.s1 - 1) / p.s1);
     const dim3 cgrid((unsigned)((ppg + kColThreads - 1) / kColThreads), (unsigned)(p.n * p.s0 * p.s1));
-    tc_dc_col2im<<<cgrid, kColThreads, 0, stream>>>(Y, x, p, c, dx);
+    switch (p.C) {
+#define PC2D_COL_CASE(k) \
+  case k: tc_dc_col2im<k><<<cgrid, kColThreads, 0, stream>>>(Y, x, p, c, dx); break;
+      PC2D_COL_CASE(1) PC2D_COL_CASE(2) PC2D_COL_CASE(3) PC2D_COL_CASE(4)
+      PC2D_COL_CASE(5) PC2D_COL_CASE(6) PC2D_COL_CASE(7) PC2D_COL_CASE(8)
+#undef PC2D_COL_CASE
+      default:
+        set_last_error("internal: unsupported channel count %d", p.C);
+        return PC2D_ERR_UNSUPPORTED;
+    }
   }
   PC2D_LAUNCH_CHECK("tc_dc_col2im");
   timing_end(K_DGRAD, stream);

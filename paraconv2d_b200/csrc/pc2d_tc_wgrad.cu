@@ -574,16 +574,19 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
 
 // Fixed-order fp64 reduction of the per-segment partials and the parameter
 // gradient epilogue:  dh = 2f dH, dp = 2f (dP - p SG), dh0 = 2f S1,
-// dp0 = -2f p0 SG.  Grid (ceil(d/64), m), 256 threads: thread (q, kx) sums
-// the segments s = q, q+4, ... of window element 64*blockIdx.x + kx, and the
-// four partials are added in the order q = 0..3, so the result does not
-// depend on timing.
-constexpr int kFinK = 64;
-__global__ void __launch_bounds__(256)
+// dp0 = -2f p0 SG.  Grid (ceil(d/32), m), 32 * fq threads: thread (q, kx)
+// sums the segments s = q, q+fq, ... of window element 32*blockIdx.x + kx
+// (eight segments' loads in flight, added in segment order), and the fq
+// partials are added in the order q = 0..fq-1, so the result does not depend
+// on timing.  The host picks the largest fq (<= 16) whose grid is resident in
+// one wave: the sum is a chain of dependent loads per thread, so its length
+// (segments / fq / 8 load latencies) sets the time.
+constexpr int kFinK = 32, kFinQ = 16;
+__global__ void __launch_bounds__(kFinK * kFinQ, 2)
 tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums, const float *__restrict__ pars,
-                  Problem p, WgCfg c, double f2, float *__restrict__ dpars) {
+                  Problem p, WgCfg c, int fq, double f2, float *__restrict__ dpars) {
   __shared__ double s_sums[2];
-  __shared__ double s_part[2][4][kFinK];
+  __shared__ double s_part[2][kFinQ][kFinK];
   const int j = blockIdx.y;
   const int kx = threadIdx.x % kFinK, q = threadIdx.x / kFinK;
   const int64_t k = (int64_t)blockIdx.x * kFinK + kx;
@@ -592,10 +595,23 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
   const int per = c.nNR * c.nmb;
   if (threadIdx.x < 32) {
     double a = 0.0, b = 0.0;
-    for (int64_t s = threadIdx.x; s < c.nseg; s += 32) {
-      const int64_t item = s * per + mb;  // nr = 0 slice carries the row sums
-      a += (double)sums[item * 128 + r1];
-      b += (double)sums[item * 128 + r2];
+    // loads of four segments first, then the adds in segment order
+    for (int64_t s0 = threadIdx.x; s0 < c.nseg; s0 += 4 * 32) {
+      float va[4], vb[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t s = s0 + 32 * u;
+        const int64_t item = s * per + mb;  // nr = 0 slice carries the row sums
+        va[u] = s < c.nseg ? sums[item * 128 + r1] : 0.f;
+        vb[u] = s < c.nseg ? sums[item * 128 + r2] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (s0 + 32 * u < c.nseg) {
+          a += (double)va[u];
+          b += (double)vb[u];
+        }
+      }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
@@ -612,10 +628,25 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
   if (k < d) {
     const int nr = (int)(k / c.NR);
     const int kl = (int)(k - (int64_t)nr * c.NR);
-    for (int64_t s = q; s < c.nseg; s += 4) {
-      const int64_t item = (s * c.nNR + nr) * c.nmb + mb;
-      ah += (double)part[(item * 128 + r1) * c.NR + kl];
-      ap += (double)part[(item * 128 + r2) * c.NR + kl];
+    // consecutive segments of one element are this far apart (floats)
+    const int64_t sstride = (int64_t)c.nNR * c.nmb * 128 * c.NR;
+    const float *sh = part + ((int64_t)nr * c.nmb + mb) * 128 * c.NR + (int64_t)r1 * c.NR + kl;
+    const float *sp = sh + (int64_t)(r2 - r1) * c.NR;
+    for (int64_t s0 = q; s0 < c.nseg; s0 += 8 * fq) {
+      float vh[8], vp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t s = s0 + (int64_t)fq * u;
+        vh[u] = s < c.nseg ? sh[s * sstride] : 0.f;
+        vp[u] = s < c.nseg ? sp[s * sstride] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (s0 + (int64_t)fq * u < c.nseg) {
+          ah += (double)vh[u];
+          ap += (double)vp[u];
+        }
+      }
     }
   }
   s_part[0][q][kx] = ah;
@@ -627,8 +658,11 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
   const float *p0 = pp + (int64_t)m * d;
   float *dh0 = dpars, *dh = dpars + m, *dpp = dh + (int64_t)m * d, *dp0 = dpp + (int64_t)m * d;
   if (q == 0 && k < d) {
-    const double th = ((s_part[0][0][kx] + s_part[0][1][kx]) + s_part[0][2][kx]) + s_part[0][3][kx];
-    const double tp = ((s_part[1][0][kx] + s_part[1][1][kx]) + s_part[1][2][kx]) + s_part[1][3][kx];
+    double th = s_part[0][0][kx], tp = s_part[1][0][kx];
+    for (int qq = 1; qq < fq; ++qq) {
+      th += s_part[0][qq][kx];
+      tp += s_part[1][qq][kx];
+    }
     const int64_t wi = (int64_t)j * d + k;
     dh[wi] = (float)(f2 * th);
     dpp[wi] = (float)(f2 * (tp - (double)pp[wi] * sg));
@@ -701,7 +735,9 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   timing_end(K_WGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
   const dim3 fgrid(ceil_div(p.d, kFinK), p.m);
-  tc_wgrad_finalize<<<fgrid, 256, 0, stream>>>(part, sums, pars, p, c, 2.0 * (double)(float)factor, dpars);
+  int fq = kFinQ;
+  while (fq > 2 && (int64_t)fgrid.x * fgrid.y * kFinK * fq > (int64_t)device_sm_count() * 1792) fq /= 2;
+  tc_wgrad_finalize<<<fgrid, kFinK * fq, 0, stream>>>(part, sums, pars, p, c, fq, 2.0 * (double)(float)factor, dpars);
   PC2D_LAUNCH_CHECK("tc_wgrad_finalize");
   return PC2D_OK;
 }
