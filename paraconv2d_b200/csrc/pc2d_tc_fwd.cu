@@ -35,8 +35,9 @@
 //   lo 32 | hi 32 | lo 32) with 64-K stages, 4 x (hi 32 | lo 32) with 32-K
 //   stages.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over work items):
-//   warps 0-3 producers, 4-7 epilogue, 8 MMA issuer (and TMEM owner),
+// Warp roles (448 threads, one CTA per SM, persistent over work items):
+//   warps 0-3 producers, 4-7 and 10-13 epilogue (two warps per TMEM lane
+//   quarter, half of the channels each), 8 MMA issuer (and TMEM owner),
 //   9 loader.  Every barrier wait is bounded in time; a wait that gives up
 //   records PC2D_ERR_TIMEOUT, raises a CTA-wide abort flag, and the CTA
 //   drains its in-flight copies and MMAs and exits.
@@ -61,7 +62,7 @@ constexpr int kMaxCh = 64;       // channel planes a stage may touch
 constexpr int kSlots = 2;        // partial-sum slots in TMEM
 constexpr int kMaxNB = 64;
 constexpr int kMaxD = 8192;
-constexpr int kFwdThreads = 320;
+constexpr int kFwdThreads = 448;
 constexpr int kMinSmem = 120 * 1024;  // keeps one CTA per SM (it owns all 512 TMEM columns)
 constexpr int kSmemLimit = 227 * 1024;
 constexpr uint32_t kColA = 256;       // A stages at 256 + 64 * SUB * stage: (hi 32, lo 32) per sub-stage
@@ -128,7 +129,7 @@ FwdCfg fwd_cfg(const Problem &p) {
 inline size_t fwd_bsplit_bytes(const FwdCfg &c) { return (size_t)c.ncb * c.nKB * c.bstage; }
 inline size_t fwd_smem_bytes(const Problem &p, const FwdCfg &c) {
   size_t s = 1024 + (size_t)c.nst * c.sstage + (size_t)c.nKB * kKS * 8 + (size_t)kMaxStages * kKS * 4 +
-             (size_t)kMaxStages * kMaxCh * 4 + 2 * kTileM * 4 + 4 * 2 * 64 * 4 + 24 * 8 + 64;
+             (size_t)kMaxStages * kMaxCh * 4 + 2 * kTileM * 4 + 8 * 2 * 64 * 4 + 28 * 8 + 64;
   (void)p;
   return std::max<size_t>(s, kMinSmem);
 }
@@ -217,8 +218,8 @@ struct Smem {
   int *offs;        // [stage][32 SUB] halo offset of each K of the stage (-1 = zero)
   int *lead;        // [stage][64] floats before each halo plane's first element
   float *s2buf;     // [tile buffer 2][128]
-  float *hcbuf;     // [epilogue warp 4][h0 64 | cj 64] of the item's channel block
-  uint64_t *full, *a_full, *s_empty, *gr_full, *gr_empty, *s2_full, *s2_empty, *final_bar;
+  float *hcbuf;     // [epilogue warp 8][h0 | cj of its channels, 64 each]
+  uint64_t *full, *b_full, *a_full, *s_empty, *gr_full, *gr_empty, *s2_full, *s2_empty, *final_bar;
   uint32_t *tmem_holder;
   volatile int *abort_flag;
 };
@@ -242,16 +243,17 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   S.s2buf = reinterpret_cast<float *>(S.lead + kMaxStages * kMaxCh);
   S.hcbuf = S.s2buf + 2 * kTileM;
   uint64_t *bars = reinterpret_cast<uint64_t *>(
-      (reinterpret_cast<uintptr_t>(S.hcbuf + 4 * 2 * 64) + 7) & ~(uintptr_t)7);
-  S.full = bars;            // [4] halo + B + offsets landed (loader expect_tx)
+      (reinterpret_cast<uintptr_t>(S.hcbuf + 8 * 2 * 64) + 7) & ~(uintptr_t)7);
+  S.full = bars;            // [4] halo + offsets landed (loader expect_tx)
   S.a_full = bars + 4;      // [4] A stage in TMEM (128 producer arrivals)
   S.s_empty = bars + 8;     // [4] stage consumed by the MMAs (commit)
   S.gr_full = bars + 12;    // [2] partial sum ready (commit)
-  S.gr_empty = bars + 14;   // [2] partial sum drained (128 epilogue arrivals)
+  S.gr_empty = bars + 14;   // [2] partial sum drained (256 epilogue arrivals)
   S.s2_full = bars + 16;    // [2]
   S.s2_empty = bars + 18;   // [2]
   S.final_bar = bars + 20;
-  S.tmem_holder = reinterpret_cast<uint32_t *>(bars + 21);
+  S.b_full = bars + 21;     // [4] B landed (loader expect_tx); only the MMA waits for it
+  S.tmem_holder = reinterpret_cast<uint32_t *>(bars + 25);
   S.abort_flag = reinterpret_cast<volatile int *>(S.tmem_holder + 1);
 
   for (int k = threadIdx.x; k < c.nK * kKStage; k += blockDim.x) {
@@ -265,16 +267,17 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMaxStages; ++i) {
       mbar_init(&S.full[i], 1);
+      mbar_init(&S.b_full[i], 1);
       mbar_init(&S.a_full[i], 128);
       mbar_init(&S.s_empty[i], 1);
     }
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&S.gr_full[i], 1);
-      mbar_init(&S.gr_empty[i], 128);
+      mbar_init(&S.gr_empty[i], 256);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.s2_full[i], 128);
-      mbar_init(&S.s2_empty[i], 128);
+      mbar_init(&S.s2_empty[i], 256);
     }
     mbar_init(S.final_bar, 1);
     *S.abort_flag = 0;
@@ -355,20 +358,25 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
       S.s2buf[tb * kTileM + r] = s2;
       mbar_arrive(&S.s2_full[tb]);
     }
-  } else if (warp < 8) {
+  } else if (warp < 8 || warp >= 10) {
     // ---------------------------------------------------------- epilogue
-    const int q = warp % 4;
+    // Two warps per TMEM lane quarter (warps 4-7 and 10-13; warp w reaches
+    // lanes 32*(w%4) .. +31), each draining and writing half of the block's
+    // channels.
+    constexpr int NBH = NB / 2;
+    const int q = warp % 4, half = warp >= 10 ? 1 : 0;
     const int r = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const int c0 = half * NBH;  // this warp's first channel within the block
     const float *h0 = pars;
     uint32_t grp = 0;
     int64_t li = 0;
     for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x, ++li) {
       const int64_t t = item / c.ncb;
       const int cb = (int)(item - t * c.ncb);
-      float hacc[NB], pacc[NB];
+      float hacc[NBH], pacc[NBH];
 #pragma unroll
-      for (int j = 0; j < NB; ++j) hacc[j] = pacc[j] = 0.f;
+      for (int j = 0; j < NBH; ++j) hacc[j] = pacc[j] = 0.f;
       for (int gi = 0; gi < c.nGroups; ++gi, ++grp) {
         const uint32_t slot = grp % kSlots, ph = (grp / kSlots) & 1;
         if (!warp_wait(&S.gr_full[slot], ph, S.abort_flag)) {
@@ -376,37 +384,28 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           break;
         }
         tc_fence_after();
-        const uint32_t dcol = tmem + lane_off + slot * 128;
-        if constexpr (NB == 48) {
-          // 16 columns of H and of P at a time: with 96 accumulators live,
-          // 32-column loads would spill
+        const uint32_t dcol = tmem + lane_off + slot * 128 + c0;
 #pragma unroll
-          for (int jc = 0; jc < NB; jc += 16) {
-            uint32_t hv[16], pv[16];
-            tmem_ld16_nowait(dcol + jc, hv);
-            tmem_ld16_nowait(dcol + NB + jc, pv);
-            tmem_ld_wait_tie(hv, pv);
+        for (int jc = 0; jc + 16 <= NBH; jc += 16) {
+          uint32_t hv[16], pv[16];
+          tmem_ld16_nowait(dcol + jc, hv);
+          tmem_ld16_nowait(dcol + NB + jc, pv);
+          tmem_ld_wait_tie(hv, pv);
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              hacc[jc + jj] += __uint_as_float(hv[jj]);
-              pacc[jc + jj] += __uint_as_float(pv[jj]);
-            }
+          for (int jj = 0; jj < 16; ++jj) {
+            hacc[jc + jj] += __uint_as_float(hv[jj]);
+            pacc[jc + jj] += __uint_as_float(pv[jj]);
           }
-        } else {
+        }
+        if constexpr (NBH % 16 == 8) {
+          constexpr int jc = NBH - 8;
+          float hv[8], pv[8];
+          tmem_ld8(dcol + jc, hv);
+          tmem_ld8(dcol + NB + jc, pv);
 #pragma unroll
-          for (int jc = 0; jc < NB; jc += 32) {
-            uint32_t hv[32], pv[32];
-            tmem_ld32_nowait(dcol + jc, hv);
-            tmem_ld32_nowait(dcol + NB + jc, pv);
-            tmem_ld_wait_tie(hv);
-            tmem_ld_wait_tie(pv);
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-              if (jc + jj < NB) {
-                hacc[jc + jj] += __uint_as_float(hv[jj]);
-                pacc[jc + jj] += __uint_as_float(pv[jj]);
-              }
-            }
+          for (int jj = 0; jj < 8; ++jj) {
+            hacc[jc + jj] += hv[jj];
+            pacc[jc + jj] += pv[jj];
           }
         }
         tc_fence_before();
@@ -424,22 +423,21 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
       const int pix = (int)(t - nimg * c.tpi) * kTileM + r;
       const bool valid = pix < p.PQ;
       const int64_t obase = nimg * (int64_t)p.m * p.PQ + pix;
-      // h0 and |P|^2 + p0^2 of the block's channels: this warp's copy in
-      // shared memory (two per lane), then all outputs in registers, then the
-      // stores
-      float *hc = S.hcbuf + q * 2 * 64;
+      // h0 and |P|^2 + p0^2 of this warp's channels: its copy in shared
+      // memory, then all outputs in registers, then the stores
+      float *hc = S.hcbuf + (q + 4 * half) * 2 * 64;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int jj = lane + 32 * e;
-        if (jj < NB) {
-          const int j = cb * NB + jj;
+        if (jj < NBH) {
+          const int j = cb * NB + c0 + jj;
           hc[jj] = j < p.m ? __ldg(h0 + j) : 0.f;
-          hc[64 + jj] = __ldg(cj + cb * NB + jj);
+          hc[64 + jj] = __ldg(cj + cb * NB + c0 + jj);
         }
       }
       __syncwarp();
 #pragma unroll
-      for (int jj = 0; jj < NB; ++jj) {
+      for (int jj = 0; jj < NBH; ++jj) {
         const float hs = hc[jj] + hacc[jj];
         pacc[jj] = factor * (fmaf(hs, hs, -s2) + 2.f * pacc[jj] - hc[64 + jj]);
         hacc[jj] = hs;
@@ -447,8 +445,8 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
       __syncwarp();
       if (valid) {
 #pragma unroll
-        for (int jj = 0; jj < NB; ++jj) {
-          const int j = cb * NB + jj;
+        for (int jj = 0; jj < NBH; ++jj) {
+          const int j = cb * NB + c0 + jj;
           if (j < p.m) {
             const int64_t oi = obase + (int64_t)j * p.PQ;
             out[oi] = pacc[jj];
@@ -477,7 +475,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           }
         }
         const uint32_t st = it % nst, ph = (it / nst) & 1;
-        if (!warp_wait(&S.a_full[st], ph, S.abort_flag)) {
+        if (!warp_wait(&S.b_full[st], ph, S.abort_flag) || !warp_wait(&S.a_full[st], ph, S.abort_flag)) {
           ok = false;
           break;
         }
@@ -543,9 +541,10 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           }
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive_expect_tx(&S.full[st], SUB * c.bstage + (uint32_t)(c.nchs * c.PS * 4));
-            bulk_g2s(sbase, bsrc, SUB * c.bstage, &S.full[st]);
+            mbar_arrive_expect_tx(&S.full[st], (uint32_t)(c.nchs * c.PS * 4));
             tma_load_2d(hbase, &xmap, x0, (int)(tg.n * p.C + clo), &S.full[st]);
+            mbar_arrive_expect_tx(&S.b_full[st], SUB * c.bstage);
+            bulk_g2s(sbase, bsrc, SUB * c.bstage, &S.b_full[st]);
           }
           __syncwarp();
           continue;
@@ -579,14 +578,15 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
               ko.x >= 0 ? (ko.x - clo) * c.PS + S.lead[st * kMaxCh + (ko.x - clo)] + ko.y : -1;
         }
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&S.full[st], SUB * c.bstage + bytes);
-          bulk_g2s(sbase, bsrc, SUB * c.bstage, &S.full[st]);
-        }
+        if (lane == 0) mbar_arrive_expect_tx(&S.full[st], bytes);
         __syncwarp();
         for (int ci = lane; ci < nch; ci += 32) {
           const tc::BulkSpan sp = tc::bulk_span(ximg + (int64_t)(clo + ci) * p.HW, run);
           bulk_g2s(hbase + (size_t)ci * c.PS * 4, sp.src, sp.bytes, &S.full[st]);
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&S.b_full[st], SUB * c.bstage);
+          bulk_g2s(sbase, bsrc, SUB * c.bstage, &S.b_full[st]);
         }
         __syncwarp();
       }
@@ -596,6 +596,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
     for (uint32_t i = 0; i < last; ++i) {
       const uint32_t idx = it - 1 - i;
       mbar_wait(&S.full[idx % nst], (idx / nst) & 1, kWaitNs, nullptr);
+      mbar_wait(&S.b_full[idx % nst], (idx / nst) & 1, kWaitNs, nullptr);
     }
   }
 
