@@ -16,13 +16,14 @@
 // the implicit GEMM of pc2d_tc_bwd.cu runs its channel dimension as an MMA N
 // of 16 per block; this form puts C*T + 1 window columns there instead.
 //
-// GEMM kernel roles (320 threads, one CTA per SM, persistent over tiles):
+// GEMM kernel roles (448 threads, one CTA per SM, persistent over tiles):
 //   - warps 0-3, producers (one TMEM lane = one output pixel): per 32-K
 //     stage read g and hsum of 16 output channels at their pixel (from the
 //     [16 x 128] tiles the loader staged, or straight from global memory
 //     with an L2 prefetch of the next stage), form g*hsum and g, split into
 //     tf32 hi + lo and tcgen05.st them (A operand);
-//   - warps 4-7, epilogue: drain the tile's accumulator (one of two TMEM
+//   - warps 4-7 and 10-13, epilogue (two warps per TMEM lane quarter, half
+//     of the columns each): drain the tile's accumulator (one of two TMEM
 //     slots) and write Y[n][col][o] (coalesced across pixels);
 //   - warp 8, MMA: one elected lane issues Ahi*Bhi + Alo*Bhi + Ahi*Blo
 //     (N = NP) per 8-wide K step, straight-line;
@@ -52,7 +53,7 @@ constexpr int kSlots = 2;         // accumulator slots
 constexpr int kMaxNP = 192;       // GEMM N (window columns + SG, multiple of 16)
 constexpr uint32_t kColSlot = 192;  // slot s at s * 192
 constexpr uint32_t kColA = 384;     // A stage st at 384 + 64 * st
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
 constexpr int kMinSmem = 120 * 1024;
 constexpr int kSmemLimit = 227 * 1024;
 
@@ -112,6 +113,35 @@ __global__ void __launch_bounds__(256) tc_dc_prep_weights(const float *__restric
   }
 }
 
+// Epilogue of one warp: 16-column blocks C0 .. C1-1 of its 32 lanes' rows of
+// the accumulator, two blocks per wait, written to Y (column stride PQ).
+template <int C0, int C1>
+__device__ __forceinline__ void dc_drain(uint32_t dcol, float *yb, bool valid, int NY, int64_t PQ) {
+#pragma unroll
+  for (int ch = C0; ch < C1; ch += 2) {
+    const int cc = ch * 16;
+    uint32_t v[16], w[16];
+    if (ch + 1 < C1) {
+      tmem_ld16_nowait(dcol + cc, v);
+      tmem_ld16_nowait(dcol + cc + 16, w);
+      tmem_ld_wait_tie(v, w);
+    } else {
+      tmem_ld16_nowait(dcol + cc, v);
+      tmem_ld_wait_tie(v);
+    }
+    if (valid) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        if (cc + q < NY) yb[(int64_t)(cc + q) * PQ] = __uint_as_float(v[q]);
+      if (ch + 1 < C1) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          if (cc + 16 + q < NY) yb[(int64_t)(cc + 16 + q) * PQ] = __uint_as_float(w[q]);
+      }
+    }
+  }
+}
+
 template <int NP>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum, const float *__restrict__ wsB,
@@ -136,7 +166,7 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
     }
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&d_full[i], 1);
-      mbar_init(&d_empty[i], 128);
+      mbar_init(&d_empty[i], 256);
     }
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&t_full[i], 1);
@@ -228,9 +258,13 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
         mbar_arrive(&a_full[st]);
       }
     }
-  } else if (warp < 8) {
+  } else if (warp < 8 || warp >= 10) {
     // ---------------------------------------------------------- epilogue
-    const int qq = warp % 4;
+    // Two warps per TMEM lane quarter (warps 4-7 and 10-13; warp w reaches
+    // lanes 32*(w%4) .. +31), each draining and writing half of the
+    // 16-column blocks.
+    constexpr int kCh = NP / 16, kCh0 = (kCh + 1) / 2;
+    const int qq = warp % 4, half = warp >= 10 ? 1 : 0;
     const int r = qq * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qq * 32) << 16;
     uint32_t ti = 0;
@@ -245,29 +279,10 @@ tc_dc_gemm_kernel(const float *__restrict__ grad, const float *__restrict__ hsum
       const int o = (int)(t - n * c.tpi) * kTileM + r;
       float *yb = Y + n * (int64_t)c.NY * p.PQ + o;
       const uint32_t dcol = tmem + lane_off + slot * kColSlot;
-      // 32 columns per wait (16 for the last block of an odd multiple of 16)
-#pragma unroll
-      for (int cc = 0; cc < NP; cc += 32) {
-        uint32_t v[16], w[16];
-        if (cc + 16 < NP) {
-          tmem_ld16_nowait(dcol + cc, v);
-          tmem_ld16_nowait(dcol + cc + 16, w);
-          tmem_ld_wait_tie(v, w);
-        } else {
-          tmem_ld16_nowait(dcol + cc, v);
-          tmem_ld_wait_tie(v);
-        }
-        if (o < p.PQ) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q)
-            if (cc + q < c.NY) yb[(int64_t)(cc + q) * p.PQ] = __uint_as_float(v[q]);
-          if (cc + 16 < NP) {
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-              if (cc + 16 + q < c.NY) yb[(int64_t)(cc + 16 + q) * p.PQ] = __uint_as_float(w[q]);
-          }
-        }
-      }
+      if (half == 0)
+        dc_drain<0, kCh0>(dcol, yb, o < p.PQ, c.NY, p.PQ);
+      else
+        dc_drain<kCh0, kCh>(dcol, yb, o < p.PQ, c.NY, p.PQ);
       tc_fence_before();
       mbar_arrive(&d_empty[slot]);
     }
