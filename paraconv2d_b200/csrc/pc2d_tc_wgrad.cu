@@ -49,7 +49,7 @@ using tc::kWaitNs;
 using tc::warp_wait;
 
 constexpr int kChunk = 32;        // pixels per K chunk
-constexpr int kAhead = 2;         // chunks an A producer prefetches ahead (L2)
+constexpr int kAhead = 8;         // chunks an A producer prefetches ahead (L2)
 constexpr int kStages = 3;
 constexpr int kMaxSeg = 32;       // chunks per segment
 constexpr int kThreads = 576;
@@ -215,7 +215,7 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         const int64_t n = gc / c.cpi;
         const int pq0 = (int)(gc - n * c.cpi) * kChunk;
         const int npx = min(kChunk, (int)p.PQ - pq0);
-        // this row two chunks ahead: start bringing it into L2 now (one
+        // this row kAhead chunks ahead: start bringing it into L2 now (one
         // thread holds one 128-byte row of a chunk)
         if (rvalid && gc + kAhead < g1) {
           const int64_t na = (gc + kAhead) / c.cpi;
