@@ -15,15 +15,16 @@
 // The windows are flipped exactly as in the forward pass: tap (ix2, iy2) of output pixel (oy, ox)
 // reads input (oy*s0 + (k0-1-ix2)*dl0, ox*s1 + (k1-1-iy2)*dl1).
 //
-// Warp roles (352 threads):
+// Warp roles (480 threads):
 //   - warps 0-3, producers (one TMEM lane = one input pixel): per tap, locate
 //     the output pixel whose window covers the pixel, form g*hsum and g for
 //     the 16 channels of the stage from the staged planes, accumulate SG,
 //     split into tf32 hi + lo and tcgen05.st them into TMEM (A operand).  A
 //     producer reuses an A slot as soon as the MMAs that read it complete;
-//   - warps 4-7, epilogue: drain the partial sums (a fresh one per j-block of
-//     16 output channels, in one of two TMEM slots) into fp32 registers, and
-//     write
+//   - warps 4-7 and 11-14, epilogue (two warps per TMEM lane quarter, half
+//     of the channels each): drain the partial sums (a fresh one per j-block
+//     of 16 output channels, in one of two TMEM slots) into fp32 registers,
+//     and write
 //     dx = 2 * (acc - x * SG), with x copied to shared memory (cp.async) at
 //     the start of the tile;
 //   - warp 8, MMA (one thread): per 8-wide K step two MMAs
@@ -39,6 +40,7 @@
 // its loops, drains its own copies and frees TMEM, as the forward kernel
 // (pc2d_tc_fwd.cu) does.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "pc2d_tc.cuh"
@@ -58,7 +60,7 @@ constexpr int kStages = 2;       // A/B stages of kTapsPS taps (64 K) each
 constexpr int kTapsPS = 2;       // taps per stage
 constexpr int kSlots = 2;        // accumulator slots (one partial sum per j-block)
 constexpr int kMaxNC = 64;
-constexpr int kThreads = 352;
+constexpr int kThreads = 480;
 constexpr int kMinSmem = 120 * 1024;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr uint32_t kColA = 256;
@@ -81,6 +83,7 @@ struct DgCfg {
   int PSo;          // g/hsum plane stride (floats, multiple of 4)
   uint32_t bstage;  // B bytes per stage (hi + lo)
   uint32_t jslot;   // bytes of a j-block slot (32 planes), multiple of 1024
+  int tma;          // 1: a j-block's planes are two 2-D tensor copies (g planes, then hsum planes)
 };
 
 // Per-phase tables copied from DgCfg into shared memory at kernel start
@@ -145,6 +148,10 @@ DgCfg dg_cfg(const Problem &p) {
   c.PSo = (int)(((int64_t)orows * p.Q + 8 + 3) / 4 * 4);
   c.bstage = (uint32_t)(2 * c.NC * 128);  // one tap
   c.jslot = (uint32_t)align_up((size_t)2 * kJB * c.PSo * 4, 1024);
+  // the 16 g (and 16 hsum) planes of a j-block as one tensor copy each: rows
+  // of PQ floats 16-byte strided, the staged run (from the 16-byte boundary
+  // at or below its first element) at most 256 floats
+  c.tma = (p.PQ % 4 == 0 && c.PSo <= 256 && (int64_t)p.n * p.m < ((int64_t)1 << 31)) ? 1 : 0;
   return c;
 }
 
@@ -262,7 +269,8 @@ __device__ __forceinline__ void dg_gather(const float *planes, const int (&to)[2
 template <int NC>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, const float *__restrict__ hsum,
-                const float *__restrict__ wsB, Problem p, DgCfg c, float *__restrict__ dx, int *status) {
+                const float *__restrict__ wsB, Problem p, DgCfg c, const __grid_constant__ CUtensorMap gmap,
+                const __grid_constant__ CUtensorMap hmap, float *__restrict__ dx, int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -306,9 +314,9 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       mbar_init(&jfull[i], 1);
       mbar_init(&jempty[i], 128);
       mbar_init(&gr_full[i], 1);
-      mbar_init(&gr_empty[i], 128);
+      mbar_init(&gr_empty[i], 256);
       mbar_init(&sg_full[i], 128);
-      mbar_init(&sg_empty[i], 128);
+      mbar_init(&sg_empty[i], 256);
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
@@ -398,9 +406,14 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       sgbuf[tb * kTileM + r] = sg;
       mbar_arrive(&sg_full[tb]);
     }
-  } else if (warp < 8) {
+  } else if (warp < 8 || warp >= 11) {
     // ---------------------------------------------------------- epilogue
-    const int qq = warp % 4;
+    // Two warps per TMEM lane quarter (warps 4-7 and 11-14; warp w reaches
+    // lanes 32*(w%4) .. +31), each draining and writing half of the block's
+    // channels.
+    constexpr int NH = NC / 2;
+    const int qq = warp % 4, half = warp >= 11 ? 1 : 0;
+    const int c0 = half * NH;  // this warp's first channel within the block
     const int r = qq * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qq * 32) << 16;
     uint32_t grp = 0;
@@ -420,15 +433,15 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         const int ay = q / tg.cols;
         xb = tg.n * p.CHW + (int64_t)(tg.py + p.s0 * ay) * p.W + tg.px + p.s1 * (q - ay * tg.cols);
 #pragma unroll 8
-        for (int cc = 0; cc < NC; ++cc) {
+        for (int cc = c0; cc < c0 + NH; ++cc) {
           const bool have = cb * NC + cc < p.C;
           cp_async4(sx + cc * kTileM + r, have ? x + xb + (int64_t)(cb * NC + cc) * p.HW : x, have);
         }
       }
       cp_async_commit();
-      float acc[NC];
+      float acc[NH];
 #pragma unroll
-      for (int j = 0; j < NC; ++j) acc[j] = 0.f;
+      for (int j = 0; j < NH; ++j) acc[j] = 0.f;
       for (int gi = 0; gi < ngroups; ++gi, ++grp) {
         const uint32_t slot = grp % kSlots, ph = (grp / kSlots) & 1;
         if (!warp_wait(&gr_full[slot], ph, abort_flag)) {
@@ -436,17 +449,23 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           break;
         }
         tc_fence_after();
-        const uint32_t dcol = tmem + lane_off + slot * 128;
+        const uint32_t dcol = tmem + lane_off + slot * 128 + c0;
 #pragma unroll
-        for (int jc = 0; jc < NC; jc += 32) {
-          uint32_t mv[32], cv[32];
-          tmem_ld32_nowait(dcol + jc, mv);
-          tmem_ld32_nowait(dcol + NC + jc, cv);
-          tmem_ld_wait_tie(mv);
-          tmem_ld_wait_tie(cv);
+        for (int jc = 0; jc + 16 <= NH; jc += 16) {
+          uint32_t mv[16], cv[16];
+          tmem_ld16_nowait(dcol + jc, mv);
+          tmem_ld16_nowait(dcol + NC + jc, cv);
+          tmem_ld_wait_tie(mv, cv);
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj)
-            if (jc + jj < NC) acc[jc + jj] += __uint_as_float(mv[jj]) + __uint_as_float(cv[jj]);
+          for (int jj = 0; jj < 16; ++jj) acc[jc + jj] += __uint_as_float(mv[jj]) + __uint_as_float(cv[jj]);
+        }
+        if constexpr (NH % 16 == 8) {
+          constexpr int jc = NH - 8;
+          float mv[8], cv[8];
+          tmem_ld8(dcol + jc, mv);
+          tmem_ld8(dcol + NC + jc, cv);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) acc[jc + jj] += mv[jj] + cv[jj];
         }
         tc_fence_before();
         mbar_arrive(&gr_empty[slot]);
@@ -462,9 +481,9 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       cp_async_wait<0>();
       if (pv) {
 #pragma unroll
-        for (int cc = 0; cc < NC; ++cc)
-          if (cb * NC + cc < p.C)
-            dx[xb + (int64_t)(cb * NC + cc) * p.HW] = 2.f * (acc[cc] - sx[cc * kTileM + r] * sg);
+        for (int cc = 0; cc < NH; ++cc)
+          if (cb * NC + c0 + cc < p.C)
+            dx[xb + (int64_t)(cb * NC + c0 + cc) * p.HW] = 2.f * (acc[cc] - sx[(c0 + cc) * kTileM + r] * sg);
       }
     }
     cp_async_wait<0>();  // copies of an item left on an error path
@@ -584,6 +603,29 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           ok = false;
           break;
         }
+        if (c.tma) {
+          // g planes of channels jb*16 .. +15 to slots 0..15, hsum planes to
+          // slots 16..31, PSo floats each from the 16-byte boundary at or
+          // below the first staged element (rows past the image's channels
+          // are never read: their table entries are -1)
+          const int xo = tg.oylo * p.Q, x0 = xo & ~3, ld = xo - x0;
+          const int jl = lane % kJB, isH = lane / kJB;
+          const int j = jb * kJB + jl;
+          jtab[js * 2 * kJB + 2 * jl + isH] = (j < p.m && run > 0) ? (isH * kJB + jl) * c.PSo + ld : -1;
+          __syncwarp();
+          if (lane == 0) {
+            if (run > 0) {
+              uint8_t *slot = sJ + (size_t)js * c.jslot;
+              mbar_arrive_expect_tx(&jfull[js], (uint32_t)(2 * kJB * c.PSo * 4));
+              tma_load_2d(slot, &gmap, x0, (int)(tg.n * p.m + jb * kJB), &jfull[js]);
+              tma_load_2d(slot + (size_t)kJB * c.PSo * 4, &hmap, x0, (int)(tg.n * p.m + jb * kJB), &jfull[js]);
+            } else {
+              mbar_arrive(&jfull[js]);
+            }
+          }
+          __syncwarp();
+          continue;
+        }
         // lane l: plane l of the j-block = channel jb*16 + l/2, g (l even) or hsum (l odd)
         const int j = jb * kJB + lane / 2;
         const bool have = (j < p.m) && run > 0;
@@ -627,7 +669,7 @@ std::mutex g_attr_mutex;
 bool g_attr_set[64][4] = {};
 
 template <int NC>
-int launch_dgrad(const Problem &p, const DgCfg &c, const float *grad, const float *x, const float *hsum,
+int launch_dgrad(const Problem &p, DgCfg c, const float *grad, const float *x, const float *hsum,
                  const float *wsB, float *dx, int *status, cudaStream_t stream) {
   int dev = 0;
   PC2D_CUDA_CHECK(cudaGetDevice(&dev));
@@ -638,9 +680,16 @@ int launch_dgrad(const Problem &p, const DgCfg &c, const float *grad, const floa
       g_attr_set[dev][NC / 16 - 1] = true;
     }
   }
+  CUtensorMap gmap, hmap;
+  std::memset(&gmap, 0, sizeof(gmap));
+  std::memset(&hmap, 0, sizeof(hmap));
+  if (c.tma && !(encode_planes_map(grad, p.PQ, (int64_t)p.n * p.m, c.PSo, kJB, &gmap) &&
+                 encode_planes_map(hsum, p.PQ, (int64_t)p.n * p.m, c.PSo, kJB, &hmap)))
+    c.tma = 0;  // per-plane bulk copies instead (same slot size)
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
   timing_begin(K_DGRAD, stream);
-  tc_dgrad_kernel<NC><<<grid, kThreads, dg_smem_bytes(c), stream>>>(grad, x, hsum, wsB, p, c, dx, status);
+  tc_dgrad_kernel<NC><<<grid, kThreads, dg_smem_bytes(c), stream>>>(grad, x, hsum, wsB, p, c, gmap, hmap, dx,
+                                                                      status);
   timing_end(K_DGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_dgrad_kernel");
   return PC2D_OK;
