@@ -42,7 +42,7 @@ class NativeLibraryMissing(ImportError):
 def _require(path: str) -> str:
     if not os.path.exists(path):
         raise NativeLibraryMissing(
-            f"{os.path.basename(path)} is not built; run `python -m paraconv2d_b200.build` "
+            f"{os.path.basename(path)} is not built; run `python paraconv2d_b200/build.py` "
             "(there is no CPU or Python fallback for this op)")
     return path
 

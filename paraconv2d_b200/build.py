@@ -6,7 +6,8 @@
   (g++ against the installed torch, links libpc2d_sm100.so).
 
 Both are rebuilt only when a source or header is newer than the library.
-Usage: ``python -m paraconv2d_b200.build [--force] [--verbose]``.
+Usage: ``python paraconv2d_b200/build.py [--force] [--verbose]`` (run as a file: importing
+the package loads the libraries this builds).
 """
 from __future__ import annotations
 
