@@ -44,5 +44,10 @@ int device_sm_count();
 // floats, zero fill outside.  False (map unusable) when the driver entry point
 // is missing, x is not 16-byte aligned or HW*4 is not a multiple of 16.
 bool encode_planes_map(const float *x, int64_t HW, int64_t rows, int box_inner, int box_rows, CUtensorMap *map);
+// 2-D tensor map over a [rows][cols] fp32 tensor (cols % 4 == 0, 16-byte
+// aligned base) with boxes of 32 floats x box_rows rows and the 128-byte
+// swizzle: in shared memory, 16-byte chunk q of box row r lands at position
+// q ^ (r % 8) of the row's 128 bytes (box base 1024-byte aligned).
+bool encode_rows_map_sw128(const float *t, int64_t cols, int64_t rows, int box_rows, CUtensorMap *map);
 
 }  // namespace pc2d

@@ -72,6 +72,8 @@ struct WgCfg {
   int PSw;          // staged plane stride (floats, multiple of 4)
   uint32_t hstage;  // halo bytes per stage (multiple of 1024)
   int tma;          // 1: the halo of a chunk is one 2-D tensor copy [nchm][PSw] (see tc_wgrad)
+  int atma;         // 1: a chunk's g and hsum rows are two 2-D tensor copies [JM][32] (128-byte swizzled)
+  uint32_t tbytes;  // shared bytes of those tiles: 2 stages x (g, hsum) x 8 KB, or 0
 };
 
 WgCfg wg_cfg(const Problem &p, int sms) {
@@ -114,18 +116,29 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   // multiple of 16 bytes; its box is the staged plane (PSw floats from the
   // 16-byte boundary at or below the chunk's first element), at most 256.
   c.tma = (p.HW % 4 == 0 && c.PSw <= 256 && (int64_t)p.n * p.C < ((int64_t)1 << 31)) ? 1 : 0;
-  const size_t need = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256) * 4 + 16 * 8 + 64;
+  const size_t need = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256) * 4 + 28 * 8 + 64;
   if (need > (size_t)kSmemLimit) c.halo = 0;  // gather from global memory instead
   if (!c.halo) {
     c.hstage = 0;
     c.tma = 0;
   }
+  // A rows as tensor copies when the rows of g and hsum are 16-byte strided
+  // and the tiles fit next to the B and halo stages; else each A producer
+  // loads its own row
+  c.atma = 0;
+  c.tbytes = 0;
+  const size_t need2 = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256) * 4 + 28 * 8 + 64;
+  if (p.PQ % 4 == 0 && p.PQ >= kChunk && (int64_t)p.n * p.m < ((int64_t)1 << 31) &&
+      need2 + 2 * 2 * 8192 <= (size_t)kSmemLimit) {
+    c.atma = 1;
+    c.tbytes = 2 * 2 * 8192;
+  }
   return c;
 }
 
 inline size_t wg_smem_bytes(const WgCfg &c) {
-  size_t s = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * 64 * 4 + (size_t)kStages * 256 * 4 +
-             16 * 8 + 64;
+  size_t s = 1024 + (size_t)kStages * (c.bstage + c.hstage) + c.tbytes + (size_t)kStages * 64 * 4 +
+             (size_t)kStages * 256 * 4 + 28 * 8 + 64;
   return std::max<size_t>(s, kMinSmem);
 }
 
@@ -152,22 +165,26 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+template <bool ATMA>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, const float *__restrict__ hsum,
-                Problem p, WgCfg c, const __grid_constant__ CUtensorMap xmap, float *__restrict__ part,
-                float *__restrict__ sums, int *status) {
+                Problem p, WgCfg c, const __grid_constant__ CUtensorMap xmap,
+                const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap hmap,
+                float *__restrict__ part, float *__restrict__ sums, int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   uint8_t *sB = base;                                                  // kStages x bstage
   uint8_t *sH = base + (size_t)kStages * c.bstage;                     // kStages x hstage
-  int *lead = reinterpret_cast<int *>(sH + (size_t)kStages * c.hstage);  // [kStages][64]
+  uint8_t *sT = sH + (size_t)kStages * c.hstage;                      // 2 x [g tile 8 KB | hsum tile 8 KB]
+  int *lead = reinterpret_cast<int *>(sT + c.tbytes);                 // [kStages][64]
   int *roffs = lead + kStages * 64;                                    // [kStages][256]
   uint64_t *bars = reinterpret_cast<uint64_t *>(roffs + kStages * 256);
   uint64_t *a_full = bars, *a_empty = bars + 3, *b_full = bars + 6, *b_empty = bars + 9;
   uint64_t *d_full = bars + 12, *d_empty = bars + 13, *final_bar = bars + 14;
   uint64_t *h_full = bars + 15, *h_empty = bars + 18;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 21);
+  uint64_t *t_full = bars + 21, *t_empty = bars + 23;  // A tiles landed / read (128 A threads)
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 25);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   if (threadIdx.x == 0) {
@@ -181,6 +198,10 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     }
     mbar_init(d_full, 1);
     mbar_init(d_empty, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&t_full[i], 1);
+      mbar_init(&t_empty[i], 128);
+    }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -200,6 +221,7 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     // -------------------------------------------------------- A producers
     const int r = warp * 32 + lane;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t sT_addr = smem_u32(sT);
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(grad) | reinterpret_cast<uintptr_t>(hsum)) & 15) == 0 &&
                         (p.PQ % 4) == 0;
     uint32_t it = 0;
@@ -224,7 +246,35 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           if (w == 0) prefetch_l2(hsum + offa);
         }
         float v[kChunk];
-        if (rvalid) {
+        if (ATMA) {
+          // this row of the chunk's g (and hsum) tile: tile row j - mb*JM,
+          // 16-byte chunk q at position q ^ (row % 8)
+          const uint32_t ts = it & 1, tph = (it >> 1) & 1;
+          if (!warp_wait(&t_full[ts], tph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int tr = rvalid ? r - w * c.JM : 0;
+          const uint32_t gt = sT_addr + ts * 16384u + (uint32_t)tr * 128u;
+#pragma unroll
+          for (int q = 0; q < kChunk / 4; ++q) {
+            const uint32_t cq = (uint32_t)((q ^ (tr & 7)) << 4);
+            const int4 g4 = lds_v4s32(gt + cq);
+            float4 a4 = make_float4(__int_as_float(g4.x), __int_as_float(g4.y), __int_as_float(g4.z),
+                                    __int_as_float(g4.w));
+            if (w == 0) {
+              const int4 h4 = lds_v4s32(gt + 8192u + cq);
+              a4.x *= __int_as_float(h4.x);
+              a4.y *= __int_as_float(h4.y);
+              a4.z *= __int_as_float(h4.z);
+              a4.w *= __int_as_float(h4.w);
+            }
+            v[4 * q] = rvalid ? a4.x : 0.f;
+            v[4 * q + 1] = rvalid ? a4.y : 0.f;
+            v[4 * q + 2] = rvalid ? a4.z : 0.f;
+            v[4 * q + 3] = rvalid ? a4.w : 0.f;
+          }
+        } else if (rvalid) {
           const int64_t off = (n * p.m + j) * p.PQ + pq0;
           if (vec_ok && npx == kChunk) {
             const float4 *gp = reinterpret_cast<const float4 *>(grad + off);
@@ -283,6 +333,9 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&a_full[st]);
+        // the tile slot is free once the values read from it have been
+        // stored (an arrive right after the shared loads could overtake them)
+        if (ATMA) mbar_arrive(&t_empty[it & 1]);
       }
       sums[item * 128 + r] = rowsum;
     }
@@ -425,10 +478,11 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     }
   } else if (warp == 17) {
     // -------------------------------------------------------------- loader
-    // Stages, per chunk, the input rows its windows read for the channels of
-    // the item's window range (one 16-byte-rounded bulk copy per channel), and
+    // Stages, per chunk, the g and hsum tiles of the A rows (ATMA) and the
+    // input rows its windows read for the channels of the item's window range
+    // (one 16-byte-rounded bulk copy per channel, or one tensor copy), and
     // the offset of every window row of the range inside that stage.
-    if (c.halo) {
+    if (c.halo || ATMA) {
       uint32_t it = 0;
       for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
         const int64_t seg = item / per;
@@ -451,13 +505,32 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         }
         const int nch = (int)(std::min<int64_t>(kbase + c.NR, p.d) - 1) / p.T - clo + 1;
         const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
+        const int mb = (int)((item - seg * per) % c.nmb);
         for (int64_t gc = g0; gc < g1; ++gc, ++it) {
+          const ChunkGeo cg = chunk_geo(p, c, gc);
+          if (ATMA) {
+            // rows mb*JM .. +JM-1 of image n's g and hsum, pixels pq0 .. +31
+            // (zero past the end of a row)
+            const uint32_t ts = it & 1, tph = (it >> 1) & 1;
+            if (!warp_wait(&t_empty[ts], tph ^ 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              uint8_t *tb = sT + (size_t)ts * 16384;
+              const int ty = (int)(cg.n * p.m + mb * c.JM);
+              mbar_arrive_expect_tx(&t_full[ts], (uint32_t)(2 * c.JM * 128));
+              tma_load_2d(tb, &gmap, cg.pq0, ty, &t_full[ts]);
+              tma_load_2d(tb + 8192, &hmap, cg.pq0, ty, &t_full[ts]);
+            }
+            __syncwarp();
+          }
+          if (!c.halo) continue;
           const uint32_t st = it % kStages, ph = (it / kStages) & 1;
           if (!warp_wait(&h_empty[st], ph ^ 1, abort_flag)) {
             ok = false;
             break;
           }
-          const ChunkGeo cg = chunk_geo(p, c, gc);
           uint8_t *hb = sH + (size_t)st * c.hstage;
           if (c.tma) {
             // one tensor copy: channels clo .. clo+nchm-1 of image n, each
@@ -509,9 +582,14 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       }
       // Drain: the copies issued last have landed before the CTA exits.
       const uint32_t last = it < (uint32_t)kStages ? it : (uint32_t)kStages;
-      for (uint32_t i = 0; i < last; ++i) {
+      for (uint32_t i = 0; i < last && c.halo; ++i) {
         const uint32_t idx = it - 1 - i;
         mbar_wait(&h_full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
+      }
+      const uint32_t tlast = it < 2u ? it : 2u;
+      for (uint32_t i = 0; i < tlast && ATMA; ++i) {
+        const uint32_t idx = it - 1 - i;
+        mbar_wait(&t_full[idx & 1], (idx >> 1) & 1, kWaitNs, nullptr);
       }
     }
   } else {
@@ -696,6 +774,14 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   std::memset(&xmap, 0, sizeof(xmap));
   if (c.tma && !encode_planes_map(x, p.HW, (int64_t)p.n * p.C, c.PSw, c.nchm, &xmap))
     c.tma = 0;  // per-channel bulk copies instead (same layout)
+  CUtensorMap gmap, hmap;
+  std::memset(&gmap, 0, sizeof(gmap));
+  std::memset(&hmap, 0, sizeof(hmap));
+  if (c.atma && !(encode_rows_map_sw128(grad, p.PQ, (int64_t)p.n * p.m, c.JM, &gmap) &&
+                  encode_rows_map_sw128(hsum, p.PQ, (int64_t)p.n * p.m, c.JM, &hmap))) {
+    c.atma = 0;  // each A producer loads its own row instead
+    c.tbytes = 0;
+  }
   int *status = device_status_ptr();
   if (!status) {
     set_last_error("could not resolve the device status word");
@@ -708,7 +794,10 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   {
     std::lock_guard<std::mutex> lock(g_attr_mutex);
     if (dev >= 0 && dev < 64 && !g_attr_set[dev]) {
-      PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+      PC2D_CUDA_CHECK(
+          cudaFuncSetAttribute(tc_wgrad_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+      PC2D_CUDA_CHECK(
+          cudaFuncSetAttribute(tc_wgrad_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
       g_attr_set[dev] = true;
     }
   }
@@ -730,7 +819,12 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tc_wgrad_kernel, grad, x, hsum, p, c, xmap, part, sums, status));
+    if (c.atma)
+      PC2D_CUDA_CHECK(
+          cudaLaunchKernelEx(&cfg, tc_wgrad_kernel<true>, grad, x, hsum, p, c, xmap, gmap, hmap, part, sums, status));
+    else
+      PC2D_CUDA_CHECK(
+          cudaLaunchKernelEx(&cfg, tc_wgrad_kernel<false>, grad, x, hsum, p, c, xmap, gmap, hmap, part, sums, status));
   }
   timing_end(K_WGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
