@@ -30,10 +30,11 @@
 // kernel sums the slices in a fixed order in fp64 and applies the epilogue
 // above.  No floating-point atomics: the result is deterministic.
 //
-// Warp roles (576 threads, one CTA per SM): warps 0-3 A producers, 4-11 B
+// Warp roles (608 threads, one CTA per SM): warps 0-3 A producers, 4-11 B
 // producers, 12-15 epilogue, 16 MMA issuer and TMEM owner, 17 loader of the
-// input rows the B producers gather from.  All waits are bounded as in the
-// forward kernel.
+// input rows the B producers gather from, 18 loader of the A rows' g and
+// hsum tiles (when they are staged by tensor copies).  All waits are bounded
+// as in the forward kernel.
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -52,7 +53,7 @@ constexpr int kChunk = 32;        // pixels per K chunk
 constexpr int kAhead = 8;         // chunks an A producer prefetches ahead (L2)
 constexpr int kStages = 3;
 constexpr int kMaxSeg = 32;       // chunks per segment
-constexpr int kThreads = 576;
+constexpr int kThreads = 608;
 constexpr int kBWarps = 8;
 constexpr int kMinSmem = 120 * 1024;
 constexpr int kSmemLimit = 227 * 1024;
@@ -478,11 +479,11 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     }
   } else if (warp == 17) {
     // -------------------------------------------------------------- loader
-    // Stages, per chunk, the g and hsum tiles of the A rows (ATMA) and the
-    // input rows its windows read for the channels of the item's window range
-    // (one 16-byte-rounded bulk copy per channel, or one tensor copy), and
-    // the offset of every window row of the range inside that stage.
-    if (c.halo || ATMA) {
+    // Stages, per chunk, the input rows its windows read for the channels of
+    // the item's window range (one 16-byte-rounded bulk copy per channel, or
+    // one tensor copy), and the offset of every window row of the range
+    // inside that stage.
+    if (c.halo) {
       uint32_t it = 0;
       for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
         const int64_t seg = item / per;
@@ -505,27 +506,8 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         }
         const int nch = (int)(std::min<int64_t>(kbase + c.NR, p.d) - 1) / p.T - clo + 1;
         const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
-        const int mb = (int)((item - seg * per) % c.nmb);
         for (int64_t gc = g0; gc < g1; ++gc, ++it) {
           const ChunkGeo cg = chunk_geo(p, c, gc);
-          if (ATMA) {
-            // rows mb*JM .. +JM-1 of image n's g and hsum, pixels pq0 .. +31
-            // (zero past the end of a row)
-            const uint32_t ts = it & 1, tph = (it >> 1) & 1;
-            if (!warp_wait(&t_empty[ts], tph ^ 1, abort_flag)) {
-              ok = false;
-              break;
-            }
-            if (lane == 0) {
-              uint8_t *tb = sT + (size_t)ts * 16384;
-              const int ty = (int)(cg.n * p.m + mb * c.JM);
-              mbar_arrive_expect_tx(&t_full[ts], (uint32_t)(2 * c.JM * 128));
-              tma_load_2d(tb, &gmap, cg.pq0, ty, &t_full[ts]);
-              tma_load_2d(tb + 8192, &hmap, cg.pq0, ty, &t_full[ts]);
-            }
-            __syncwarp();
-          }
-          if (!c.halo) continue;
           const uint32_t st = it % kStages, ph = (it / kStages) & 1;
           if (!warp_wait(&h_empty[st], ph ^ 1, abort_flag)) {
             ok = false;
@@ -582,12 +564,44 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       }
       // Drain: the copies issued last have landed before the CTA exits.
       const uint32_t last = it < (uint32_t)kStages ? it : (uint32_t)kStages;
-      for (uint32_t i = 0; i < last && c.halo; ++i) {
+      for (uint32_t i = 0; i < last; ++i) {
         const uint32_t idx = it - 1 - i;
         mbar_wait(&h_full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
       }
+    }
+  } else if (warp == 18) {
+    // ------------------------------------------------------- A tile loader
+    // Per chunk, rows mb*JM .. +JM-1 of image n's g and hsum, pixels
+    // pq0 .. +31 (zero past the end of a row), into one of two tile slots.
+    // A warp of its own, so that these copies and the halo copies are
+    // issued side by side.
+    if (ATMA) {
+      uint32_t it = 0;
+      for (int64_t item = blockIdx.x; item < c.items && ok; item += gridDim.x) {
+        const int64_t seg = item / per;
+        const int mb = (int)((item - seg * per) % c.nmb);
+        const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
+        for (int64_t gc = g0; gc < g1; ++gc, ++it) {
+          const uint32_t ts = it & 1, tph = (it >> 1) & 1;
+          if (!warp_wait(&t_empty[ts], tph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            const int64_t n = gc / c.cpi;
+            const int pq0 = (int)(gc - n * c.cpi) * kChunk;
+            uint8_t *tb = sT + (size_t)ts * 16384;
+            const int ty = (int)(n * p.m + mb * c.JM);
+            mbar_arrive_expect_tx(&t_full[ts], (uint32_t)(2 * c.JM * 128));
+            tma_load_2d(tb, &gmap, pq0, ty, &t_full[ts]);
+            tma_load_2d(tb + 8192, &hmap, pq0, ty, &t_full[ts]);
+          }
+          __syncwarp();
+        }
+      }
+      // Drain: the copies issued last have landed before the CTA exits.
       const uint32_t tlast = it < 2u ? it : 2u;
-      for (uint32_t i = 0; i < tlast && ATMA; ++i) {
+      for (uint32_t i = 0; i < tlast; ++i) {
         const uint32_t idx = it - 1 - i;
         mbar_wait(&t_full[idx & 1], (idx >> 1) & 1, kWaitNs, nullptr);
       }
