@@ -74,6 +74,7 @@ struct WgCfg {
   uint32_t hstage;  // halo bytes per stage (multiple of 1024)
   int tma;          // 1: the halo of a chunk is one 2-D tensor copy [nchm][PSw] (see tc_wgrad)
   int atma;         // 1: a chunk's g and hsum rows are two 2-D tensor copies [JM][32] (128-byte swizzled)
+  int kst;          // B / halo stages in flight (3, or 2 to make room for the A tiles)
   uint32_t tbytes;  // shared bytes of those tiles: 2 stages x (g, hsum) x 8 KB, or 0
 };
 
@@ -117,6 +118,7 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   // multiple of 16 bytes; its box is the staged plane (PSw floats from the
   // 16-byte boundary at or below the chunk's first element), at most 256.
   c.tma = (p.HW % 4 == 0 && c.PSw <= 256 && (int64_t)p.n * p.C < ((int64_t)1 << 31)) ? 1 : 0;
+  c.kst = kStages;
   const size_t need = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256) * 4 + 28 * 8 + 64;
   if (need > (size_t)kSmemLimit) c.halo = 0;  // gather from global memory instead
   if (!c.halo) {
@@ -128,18 +130,24 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   // loads its own row
   c.atma = 0;
   c.tbytes = 0;
-  const size_t need2 = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256) * 4 + 28 * 8 + 64;
-  if (p.PQ % 4 == 0 && p.PQ >= kChunk && (int64_t)p.n * p.m < ((int64_t)1 << 31) &&
-      need2 + 2 * 2 * 8192 <= (size_t)kSmemLimit) {
-    c.atma = 1;
-    c.tbytes = 2 * 2 * 8192;
+  // (with the halo path, two B and halo stages when three leave no room)
+  if (p.PQ % 4 == 0 && p.PQ >= kChunk && (int64_t)p.n * p.m < ((int64_t)1 << 31)) {
+    for (int kst = kStages; kst >= (c.halo ? 2 : kStages); --kst) {
+      const size_t need2 = 1024 + (size_t)kst * (c.bstage + c.hstage) + (size_t)kst * (64 + 256) * 4 + 28 * 8 + 64;
+      if (need2 + 2 * 2 * 8192 <= (size_t)kSmemLimit) {
+        c.atma = 1;
+        c.tbytes = 2 * 2 * 8192;
+        c.kst = kst;
+        break;
+      }
+    }
   }
   return c;
 }
 
 inline size_t wg_smem_bytes(const WgCfg &c) {
-  size_t s = 1024 + (size_t)kStages * (c.bstage + c.hstage) + c.tbytes + (size_t)kStages * 64 * 4 +
-             (size_t)kStages * 256 * 4 + 28 * 8 + 64;
+  size_t s = 1024 + (size_t)c.kst * (c.bstage + c.hstage) + c.tbytes + (size_t)c.kst * 64 * 4 +
+             (size_t)c.kst * 256 * 4 + 28 * 8 + 64;
   return std::max<size_t>(s, kMinSmem);
 }
 
@@ -166,7 +174,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <bool ATMA>
+template <bool ATMA, int KST>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, const float *__restrict__ hsum,
                 Problem p, WgCfg c, const __grid_constant__ CUtensorMap xmap,
@@ -175,12 +183,12 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  uint8_t *sB = base;                                                  // kStages x bstage
-  uint8_t *sH = base + (size_t)kStages * c.bstage;                     // kStages x hstage
-  uint8_t *sT = sH + (size_t)kStages * c.hstage;                      // 2 x [g tile 8 KB | hsum tile 8 KB]
-  int *lead = reinterpret_cast<int *>(sT + c.tbytes);                 // [kStages][64]
-  int *roffs = lead + kStages * 64;                                    // [kStages][256]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(roffs + kStages * 256);
+  uint8_t *sB = base;                                                  // KST x bstage
+  uint8_t *sH = base + (size_t)KST * c.bstage;                     // KST x hstage
+  uint8_t *sT = sH + (size_t)KST * c.hstage;                      // 2 x [g tile 8 KB | hsum tile 8 KB]
+  int *lead = reinterpret_cast<int *>(sT + c.tbytes);                 // [KST][64]
+  int *roffs = lead + KST * 64;                                    // [KST][256]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(roffs + KST * 256);
   uint64_t *a_full = bars, *a_empty = bars + 3, *b_full = bars + 6, *b_empty = bars + 9;
   uint64_t *d_full = bars + 12, *d_empty = bars + 13, *final_bar = bars + 14;
   uint64_t *h_full = bars + 15, *h_empty = bars + 18;
@@ -189,7 +197,7 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < KST; ++i) {
       mbar_init(&a_full[i], 128);
       mbar_init(&a_empty[i], 1);
       mbar_init(&b_full[i], kBWarps);
@@ -320,7 +328,7 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           hi[q] = tf32_hi_bits(v[q]);
           lo[q] = __float_as_uint(v[q] - __uint_as_float(hi[q]));
         }
-        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        const uint32_t st = it % KST, ph = (it / KST) & 1;
         if (!warp_wait(&a_empty[st], ph ^ 1, abort_flag)) {
           ok = false;
           break;
@@ -368,7 +376,7 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         const int pq = cg.pq0 + lane;
         const bool pvalid = lane < cg.npx;
         const int oy = pq / p.Q, ox = pq - (pq / p.Q) * p.Q;
-        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        const uint32_t st = it % KST, ph = (it / KST) & 1;
         if (c.halo && !warp_wait(&h_full[st], ph, abort_flag)) {
           ok = false;
           break;
@@ -508,7 +516,7 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
         for (int64_t gc = g0; gc < g1; ++gc, ++it) {
           const ChunkGeo cg = chunk_geo(p, c, gc);
-          const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+          const uint32_t st = it % KST, ph = (it / KST) & 1;
           if (!warp_wait(&h_empty[st], ph ^ 1, abort_flag)) {
             ok = false;
             break;
@@ -563,10 +571,10 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         }
       }
       // Drain: the copies issued last have landed before the CTA exits.
-      const uint32_t last = it < (uint32_t)kStages ? it : (uint32_t)kStages;
+      const uint32_t last = it < (uint32_t)KST ? it : (uint32_t)KST;
       for (uint32_t i = 0; i < last; ++i) {
         const uint32_t idx = it - 1 - i;
-        mbar_wait(&h_full[idx % kStages], (idx / kStages) & 1, kWaitNs, nullptr);
+        mbar_wait(&h_full[idx % KST], (idx / KST) & 1, kWaitNs, nullptr);
       }
     }
   } else if (warp == 18) {
@@ -619,7 +627,7 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       const int64_t seg = item / per;
       const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
       for (int64_t gc = g0; gc < g1; ++gc, ++it) {
-        const uint32_t st = it % kStages, ph = (it / kStages) & 1;
+        const uint32_t st = it % KST, ph = (it / KST) & 1;
         if (!warp_wait(&a_full[st], ph, abort_flag) || !warp_wait(&b_full[st], ph, abort_flag)) {
           ok = false;
           break;
@@ -795,6 +803,7 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
                   encode_rows_map_sw128(hsum, p.PQ, (int64_t)p.n * p.m, c.JM, &hmap))) {
     c.atma = 0;  // each A producer loads its own row instead
     c.tbytes = 0;
+    c.kst = kStages;
   }
   int *status = device_status_ptr();
   if (!status) {
@@ -809,9 +818,11 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
     std::lock_guard<std::mutex> lock(g_attr_mutex);
     if (dev >= 0 && dev < 64 && !g_attr_set[dev]) {
       PC2D_CUDA_CHECK(
-          cudaFuncSetAttribute(tc_wgrad_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+          cudaFuncSetAttribute(tc_wgrad_kernel<false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
       PC2D_CUDA_CHECK(
-          cudaFuncSetAttribute(tc_wgrad_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+          cudaFuncSetAttribute(tc_wgrad_kernel<true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+      PC2D_CUDA_CHECK(
+          cudaFuncSetAttribute(tc_wgrad_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
       g_attr_set[dev] = true;
     }
   }
@@ -833,12 +844,15 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (c.atma)
+    if (c.atma && c.kst == 2)
       PC2D_CUDA_CHECK(
-          cudaLaunchKernelEx(&cfg, tc_wgrad_kernel<true>, grad, x, hsum, p, c, xmap, gmap, hmap, part, sums, status));
+          cudaLaunchKernelEx(&cfg, tc_wgrad_kernel<true, 2>, grad, x, hsum, p, c, xmap, gmap, hmap, part, sums, status));
+    else if (c.atma)
+      PC2D_CUDA_CHECK(
+          cudaLaunchKernelEx(&cfg, tc_wgrad_kernel<true, 3>, grad, x, hsum, p, c, xmap, gmap, hmap, part, sums, status));
     else
-      PC2D_CUDA_CHECK(
-          cudaLaunchKernelEx(&cfg, tc_wgrad_kernel<false>, grad, x, hsum, p, c, xmap, gmap, hmap, part, sums, status));
+      PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tc_wgrad_kernel<false, 3>, grad, x, hsum, p, c, xmap, gmap, hmap, part,
+                                         sums, status));
   }
   timing_end(K_WGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
