@@ -147,7 +147,8 @@ DgCfg dg_cfg(const Problem &p) {
   c.items = c.tiles * c.ncb;
   c.PSo = (int)(((int64_t)orows * p.Q + 8 + 3) / 4 * 4);
   c.bstage = (uint32_t)(2 * c.NC * 128);  // one tap
-  c.jslot = (uint32_t)align_up((size_t)2 * kJB * c.PSo * 4, 1024);
+  // 32 planes, then one plane of zeros that missing channels point at
+  c.jslot = (uint32_t)align_up((size_t)(2 * kJB + 1) * c.PSo * 4, 1024);
   // the 16 g (and 16 hsum) planes of a j-block as one tensor copy each: rows
   // of PQ floats 16-byte strided, the staged run (from the 16-byte boundary
   // at or below its first element) at most 256 floats
@@ -248,15 +249,15 @@ __device__ __forceinline__ int2 dg_tap_entry(const Problem &p, const DgCfg &c, c
 }
 
 // 32 A values of one tap for this pixel: {g*hsum, g} of the j-block's 16
-// channels at the output pixel ooff of the staged planes, split into tf32
-// hi + lo; accumulates SG.
+// channels at the output pixel ooff of the staged planes (a channel past m
+// reads the slot's zero plane), split into tf32 hi + lo; accumulates SG.
 __device__ __forceinline__ void dg_gather(const float *planes, const int (&to)[2 * kJB], bool valid, int ooff,
                                           float &sg, uint32_t (&hi)[kKS], uint32_t (&lo)[kKS]) {
 #pragma unroll
   for (int jl = 0; jl < kJB; ++jl) {
     const int og = to[2 * jl], oh = to[2 * jl + 1];
-    const float gv = (valid && og >= 0) ? planes[og + ooff] : 0.f;
-    const float hv = (valid && oh >= 0) ? planes[oh + ooff] : 0.f;
+    const float gv = valid ? planes[og + ooff] : 0.f;
+    const float hv = valid ? planes[oh + ooff] : 0.f;
     sg += gv;
     const float a0 = gv * hv, a1 = gv;
     hi[2 * jl] = tf32_hi_bits(a0);
@@ -277,7 +278,7 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   uint8_t *sB = base;                                                 // [kStages][kTapsPS] x bstage
   uint8_t *sJ = base + (size_t)kStages * kTapsPS * c.bstage;          // 2 x jslot
   float *sx = reinterpret_cast<float *>(sJ + 2 * (size_t)c.jslot);    // [NC][128] input values of the tile
-  int *jtab = reinterpret_cast<int *>(sx + NC * kTileM);              // [2][32] plane offsets (-1 = zero)
+  int *jtab = reinterpret_cast<int *>(sx + NC * kTileM);              // [2][32] plane offsets (missing planes: the zero plane)
   float *sgbuf = reinterpret_cast<float *>(jtab + 2 * 2 * kJB);       // [2][128]
   uint64_t *bars = reinterpret_cast<uint64_t *>((reinterpret_cast<uintptr_t>(sgbuf + 2 * kTileM) + 7) & ~(uintptr_t)7);
   uint64_t *a_full = bars, *s_empty = bars + 2, *jfull = bars + 4, *jempty = bars + 6;
@@ -303,6 +304,9 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   }
   __syncthreads();
   for (int e = threadIdx.x; e < p.T; e += blockDim.x) ptab[e] = dg_tap_entry(p, c, ps, e);
+  // the zero plane after the 32 planes of each j-block slot (no copy writes it)
+  for (int e = threadIdx.x; e < 2 * c.PSo; e += blockDim.x)
+    reinterpret_cast<float *>(sJ + (size_t)(e / c.PSo) * c.jslot)[2 * kJB * c.PSo + e % c.PSo] = 0.f;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       // 128 producer arrivals + the weight loader's arrival with the bytes of
@@ -611,7 +615,7 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           const int xo = tg.oylo * p.Q, x0 = xo & ~3, ld = xo - x0;
           const int jl = lane % kJB, isH = lane / kJB;
           const int j = jb * kJB + jl;
-          jtab[js * 2 * kJB + 2 * jl + isH] = (j < p.m && run > 0) ? (isH * kJB + jl) * c.PSo + ld : -1;
+          jtab[js * 2 * kJB + 2 * jl + isH] = (j < p.m && run > 0) ? (isH * kJB + jl) * c.PSo + ld : 2 * kJB * c.PSo;
           __syncwarp();
           if (lane == 0) {
             if (run > 0) {
@@ -636,7 +640,7 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           sp = tc::bulk_span(src, run);
           bytes = sp.bytes;
         }
-        jtab[js * 2 * kJB + lane] = have ? lane * c.PSo + sp.lead : -1;
+        jtab[js * 2 * kJB + lane] = have ? lane * c.PSo + sp.lead : 2 * kJB * c.PSo;
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
         __syncwarp();
