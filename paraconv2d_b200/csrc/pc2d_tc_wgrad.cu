@@ -225,6 +225,9 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   const uint32_t tmem = *tmem_holder;
   const int per = c.nNR * c.nmb;
   bool ok = true;
+  // the reduction launched after this grid waits for it to complete; let it
+  // be scheduled as this grid's CTAs finish
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp < 4) {
     // -------------------------------------------------------- A producers
@@ -670,6 +673,12 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  // This grid may have started while the input-gradient kernel before it
+  // was still running (programmatic launch).  It ends only after that kernel
+  // has completed and its writes are visible, so that the work after this
+  // one on the stream (the reduction, then the caller's use of dx) never
+  // overtakes it.  A no-op after an ordinary launch.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // Fixed-order fp64 reduction of the per-segment partials and the parameter
@@ -687,6 +696,9 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
                   Problem p, WgCfg c, int fq, double f2, float *__restrict__ dpars) {
   __shared__ double s_sums[2];
   __shared__ double s_part[2][kFinQ][kFinK];
+  // launched as a programmatic dependent of the parameter-gradient kernel:
+  // its partials are complete and visible only after this wait
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int j = blockIdx.y;
   const int kx = threadIdx.x % kFinK, q = threadIdx.x / kFinK;
   const int64_t k = (int64_t)blockIdx.x * kFinK + kx;
@@ -832,7 +844,9 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   // this one on the stream, this grid may start on the SMs it has left (it
   // reads none of that kernel's outputs, and their workspace regions are
   // disjoint; everything earlier on the stream has completed before that
-  // kernel's own launch).  After any other kernel it starts as usual.
+  // kernel's own launch), and waits for it to complete before it ends
+  // (griddepcontrol.wait at the end of the kernel).  After any other kernel
+  // it starts as usual.
   {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -859,7 +873,20 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   const dim3 fgrid(ceil_div(p.d, kFinK), p.m);
   int fq = kFinQ;
   while (fq > 2 && (int64_t)fgrid.x * fgrid.y * kFinK * fq > (int64_t)device_sm_count() * 1792) fq /= 2;
-  tc_wgrad_finalize<<<fgrid, kFinK * fq, 0, stream>>>(part, sums, pars, p, c, fq, 2.0 * (double)(float)factor, dpars);
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = fgrid;
+    cfg.blockDim = dim3(kFinK * fq);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tc_wgrad_finalize, part, sums, pars, p, c, fq,
+                                       2.0 * (double)(float)factor, dpars));
+  }
   PC2D_LAUNCH_CHECK("tc_wgrad_finalize");
   return PC2D_OK;
 }
