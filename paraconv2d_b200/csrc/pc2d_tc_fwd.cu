@@ -129,7 +129,7 @@ FwdCfg fwd_cfg(const Problem &p) {
 inline size_t fwd_bsplit_bytes(const FwdCfg &c) { return (size_t)c.ncb * c.nKB * c.bstage; }
 inline size_t fwd_smem_bytes(const Problem &p, const FwdCfg &c) {
   size_t s = 1024 + (size_t)c.nst * c.sstage + (size_t)c.nKB * kKS * 8 + (size_t)kMaxStages * kKS * 4 +
-             (size_t)kMaxStages * kMaxCh * 4 + 2 * kTileM * 4 + 8 * 2 * 64 * 4 + 28 * 8 + 64;
+             (size_t)kMaxStages * kMaxCh * 4 + 2 * kTileM * 4 + 8 * 2 * 64 * 4 + (size_t)c.PS * 4 + 16 + 28 * 8 + 64;
   (void)p;
   return std::max<size_t>(s, kMinSmem);
 }
@@ -215,10 +215,11 @@ __device__ __forceinline__ TileGeo tile_geo(const Problem &p, const FwdCfg &c, i
 struct Smem {
   uint8_t *stage;   // nst x [SUB x (B hi | B lo) | halo planes]
   int2 *koff;       // per K: (channel, tap offset row*W + col), channel -1 past d
-  int *offs;        // [stage][32 SUB] halo offset of each K of the stage (-1 = zero)
+  int *offs;        // [stage][32 SUB] halo offset of each K of the stage (past the window: zbuf)
   int *lead;        // [stage][64] floats before each halo plane's first element
   float *s2buf;     // [tile buffer 2][128]
   float *hcbuf;     // [epilogue warp 8][h0 | cj of its channels, 64 each]
+  float *zbuf;      // PS zeros: window entries past the window point here
   uint64_t *full, *b_full, *a_full, *s_empty, *gr_full, *gr_empty, *s2_full, *s2_empty, *final_bar;
   uint32_t *tmem_holder;
   volatile int *abort_flag;
@@ -242,8 +243,9 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
   S.lead = S.offs + kMaxStages * kKS;
   S.s2buf = reinterpret_cast<float *>(S.lead + kMaxStages * kMaxCh);
   S.hcbuf = S.s2buf + 2 * kTileM;
+  S.zbuf = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(S.hcbuf + 8 * 2 * 64) + 15) & ~(uintptr_t)15);
   uint64_t *bars = reinterpret_cast<uint64_t *>(
-      (reinterpret_cast<uintptr_t>(S.hcbuf + 8 * 2 * 64) + 7) & ~(uintptr_t)7);
+      (reinterpret_cast<uintptr_t>(S.hcbuf + 8 * 2 * 64 + c.PS + 4) + 7) & ~(uintptr_t)7);
   S.full = bars;            // [4] halo + offsets landed (loader expect_tx)
   S.a_full = bars + 4;      // [4] A stage in TMEM (128 producer arrivals)
   S.s_empty = bars + 8;     // [4] stage consumed by the MMAs (commit)
@@ -283,6 +285,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
     *S.abort_flag = 0;
     fence_mbar_init();
   }
+  for (int e = threadIdx.x; e < c.PS; e += blockDim.x) S.zbuf[e] = 0.f;
   if (warp == 8) {
     tmem_alloc(S.tmem_holder, 512);
     tmem_relinquish();
@@ -331,7 +334,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
           }
           float v[32];
 #pragma unroll
-          for (int kk = 0; kk < 32; ++kk) v[kk] = (valid && o[kk] >= 0) ? halo[o[kk] + poff] : 0.f;
+          for (int kk = 0; kk < 32; ++kk) v[kk] = valid ? halo[o[kk] + poff] : 0.f;
           uint32_t hi[32], lo[32];
 #pragma unroll
           for (int kk = 0; kk < 32; ++kk) {
@@ -528,6 +531,9 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
         const int clo = S.koff[kq * kKStage].x;
         uint8_t *sbase = S.stage + (size_t)st * c.sstage;
         uint8_t *hbase = sbase + SUB * c.bstage;
+        // entries past the window read the zero buffer (relative to this
+        // stage's halo, where the producers add the pixel's offset)
+        const int zoff = (int)(S.zbuf - reinterpret_cast<const float *>(hbase));
         const float *bsrc = wsB + ((int64_t)cb * c.nKB + (int64_t)kq * SUB) * 2 * c.N * 32;
         if (c.tma) {
           // one tensor copy: planes clo .. clo+nchs-1 of image n, PS floats
@@ -537,7 +543,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
 #pragma unroll
           for (int e = 0; e < kKStage / 32; ++e) {
             const int2 ko = S.koff[kq * kKStage + lane + 32 * e];
-            S.offs[st * kKStage + lane + 32 * e] = ko.x >= 0 ? (ko.x - clo) * c.PS + ld + ko.y : -1;
+            S.offs[st * kKStage + lane + 32 * e] = ko.x >= 0 ? (ko.x - clo) * c.PS + ld + ko.y : zoff;
           }
           __syncwarp();
           if (lane == 0) {
@@ -575,7 +581,7 @@ tc_forward_kernel(const float *__restrict__ x, const float *__restrict__ pars, c
         for (int e = 0; e < kKStage / 32; ++e) {
           const int2 ko = S.koff[kq * kKStage + lane + 32 * e];
           S.offs[st * kKStage + lane + 32 * e] =
-              ko.x >= 0 ? (ko.x - clo) * c.PS + S.lead[st * kMaxCh + (ko.x - clo)] + ko.y : -1;
+              ko.x >= 0 ? (ko.x - clo) * c.PS + S.lead[st * kMaxCh + (ko.x - clo)] + ko.y : zoff;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive_expect_tx(&S.full[st], bytes);
