@@ -2,36 +2,45 @@
 """Throughput of the ParaConv2d layer on B200: forward and forward+backward
 images/s on the 64->64-channel, 32x32, k3 layer with a batch of 128 images
 per GPU (fp32, seeded synthetic data), plus the fraction of the op's
-tensor-core roofline.
+tensor-core roofline; and the data-parallel training step of the 4-layer
+stack (3->32->64->64->64, 64x64 input, global batch 1024 split across the
+GPUs) in the same line.
 
-A "step" is one forward + backward pass of the layer over the per-GPU batch
-(with --gpus N > 1, followed by an NCCL all-reduce of the parameter
-gradient, the data-parallel training step; scaling is weak: 128 images per
-GPU).  Output: one JSON line on rank 0.
+A "step" of the headline is one forward + backward pass of the layer over
+the per-GPU batch (with --gpus N > 1, followed by an NCCL all-reduce of the
+parameter gradient; scaling is weak: 128 images per GPU).  Output: one JSON
+line on rank 0.
 
   value     fwd+bwd images/s over all GPUs, inputs resident in HBM, through
             the C ABI (include/paraconv2d.h); L2 flushed before every step,
             outside the timed events
   e2e       the same through the public module (ParaConv2d forward +
             autograd backward), with the step's input and upstream gradient
-            copied from pinned host memory and the parameter gradient read
-            back, all inside the timed region
+            copied from pinned host memory and the output, the input gradient
+            and the parameter gradient copied back, all inside the timed
+            region
   roofline  the dominant kernel (largest summed CUDA-event time, timed per
             launch by the library's pc2d_timing_* hooks in a second timed
             pass of the same steps; the hooks stay off in the pass that gives
             value, because their events cost ~20 us per step and keep wgrad
             from starting while dgrad finishes) against the 3xTF32 tensor
             peak (a measured TF32 GEMM rate / 3)
-  cpu_baseline  the reference CPU op on the host cores (bounded sample)
+  cpu_baseline  the reference CPU op on the host cores (bounded sample; N=1)
+  dp_step   the stack's data-parallel training step (strong scaling): its
+            images/s, the all-reduce time, and a check on rank 0 that the
+            all-reduced gradients equal those of the whole batch computed in
+            one process
 
 --impl reference times the reference's own CPU implementation of the op
 (built from its sources into oracle/_ref; the oracle port where that build
-is absent) on the host cores, same metric and workload.
+is absent) on the host cores, same metric and workload: each step is the
+forward + backward of one image per host thread.
 """
 from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
+import importlib.util
 import json
 import os
 import statistics
@@ -45,33 +54,55 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-WORKLOAD = "c2"
-METRIC = "fwd & fwd+bwd images/s (N=128, 64→64ch, 32×32, k3) on B200; % of roofline"
 UNIT = "images/s"
 L2_FLUSH_BYTES = 512 << 20
+STACK = "c5"
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
-# each main kernel on the c2 layer, from the ncu --set full capture summarised
-# in profiles/tc_kernels_c2.md.  Writes that are still in L2 when a kernel ends
+# each main kernel on the c2 layer, from one ncu capture of those kernels
+# (the command is in TRAFFIC_SOURCE).  Writes still in L2 when a kernel ends
 # are not counted by that capture.
 NCU_TRAFFIC_BYTES = {
     ("c2", "forward"): 38.542336e6 + 13.854464e6,
     ("c2", "dgrad"): 105.669376e6 + 16.545280e6,
     ("c2", "wgrad"): 105.206016e6 + 14.017024e6,
 }
+TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:tc_(forward|dgrad|wgrad)_kernel -c 3 on the c2 layer "
+                  "(pc2d_forward + pc2d_backward of the seeded workload through the C ABI), not this run")
 
 # Kernel families the library can time (pc2d_timing_read).
 KERNELS = ("forward", "dgrad", "wgrad", "simt_forward", "simt_dgrad", "simt_wgrad")
 
 
+def load_workloads():
+    """paraconv2d_b200/workloads.py by path: importing the package would load
+    the op libraries, which the reference arm must not do."""
+    name = "pc2d_bench_workloads"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, "paraconv2d_b200", "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def metric_of(wl):
+    if len(wl.layers) > 1:
+        return f"{wl.name} data-parallel training step images/s ({wl.description})"
+    return f"fwd & fwd+bwd images/s ({wl.description}) on B200; % of roofline"
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default=WORKLOAD)
+    ap.add_argument("--workload", default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-stack", action="store_true", help="skip the data-parallel stack block")
+    ap.add_argument("--stack-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU work of the baseline sample")
     return ap.parse_args()
 
@@ -102,8 +133,9 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.lines = []
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -112,8 +144,7 @@ class ClockSampler:
             self.proc = None
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def stop(self):
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -123,12 +154,12 @@ class ClockSampler:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.lines = [l for l in out.splitlines() if l.strip()]
-        return False
+            self.proc = None
 
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
+        for line in self.lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -180,105 +211,157 @@ def measure_tf32_tflops(device):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+class Dist:
+    """The process group of a torchrun launch (None at N=1), with the helpers
+    every rank calls in the same order."""
+
+    def __init__(self, world, dev):
+        self.pg = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+            self.pg = dist
+        self.dev = dev
+
+    def barrier(self):
+        if self.pg is not None:
+            self.pg.barrier()
+
+    def max(self, v):
+        if self.pg is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=self.dev)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_reduce(self, t):
+        if self.pg is not None:
+            self.pg.all_reduce(t)
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
 # --------------------------------------------------------- CPU reference arm
 
-def cpu_reference_rate(wl, cpu_seconds, threads):
-    """images/s of the reference CPU op (fwd+bwd and fwd) on `threads` host
-    threads, one image per task; the sample is sized to ~cpu_seconds of work."""
-    import numpy as np
-
+def cpu_reference_step(wl, threads, use_ref):
+    """One reference step on the host: forward + backward of `threads` images
+    of the layer, one image per thread (the reference op is single-threaded
+    and releases the GIL).  Returns (seconds, images, kind)."""
     import oracle
-    from paraconv2d_b200 import workloads
 
+    workloads = load_workloads()
     L = wl.layer
-    x, pars, g = workloads.draw(wl, n=None)
-    grad = workloads.draw_grad(wl, g)
-    xp = workloads.pad_input(x, L.p)
-    use_ref = oracle.load_reference()
+    if not hasattr(cpu_reference_step, "cache"):
+        x, pars, g = workloads.draw(wl, n=None)
+        grad = workloads.draw_grad(wl, g)
+        cpu_reference_step.cache = (workloads.pad_input(x, L.p), pars[0], grad)
+        cpu_reference_step.next = 0
+    xp, pars, grad = cpu_reference_step.cache
+    if use_ref:
+        oracle.load_reference()
     kind = "reference" if use_ref else "port"
 
-    def one(i, with_bwd=True):
+    def one(i):
         xi = xp[i:i + 1].contiguous()
         if use_ref:
-            out, hs = oracle.ref_forward(xi, pars[0], 1.0, L.k, L.s, 1)
-            if with_bwd:
-                oracle.ref_backward(grad[i:i + 1].contiguous(), xi, pars[0], hs, 1.0, L.k, L.s, 1, False)
+            out, hs = oracle.ref_forward(xi, pars, 1.0, L.k, L.s, 1)
+            oracle.ref_backward(grad[i:i + 1].contiguous(), xi, pars, hs, 1.0, L.k, L.s, 1, False)
         else:
             xn = xi.numpy()
-            out, hs = oracle.forward(xn, pars[0].numpy(), 1.0, L.k, L.s, 1)
-            if with_bwd:
-                oracle.backward(grad[i:i + 1].numpy(), xn, pars[0].numpy(), hs, 1.0, L.k, L.s, 1, False)
+            out, hs = oracle.forward(xn, pars.numpy(), 1.0, L.k, L.s, 1)
+            oracle.backward(grad[i:i + 1].numpy(), xn, pars.numpy(), hs, 1.0, L.k, L.s, 1, False)
 
-    # calibrate on one image, single thread
-    t0 = time.perf_counter()
-    one(0)
-    t1 = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    one(0, with_bwd=False)
-    tf1 = time.perf_counter() - t0
-    n_img = int(max(threads, min(wl.n, round(cpu_seconds / max(t1, 1e-6)))))
-    n_img = max(threads, (n_img // threads) * threads)
-    idx = [i % wl.n for i in range(n_img)]
+    idx = [(cpu_reference_step.next + i) % wl.n for i in range(threads)]
+    cpu_reference_step.next = (cpu_reference_step.next + threads) % wl.n
     with cf.ThreadPoolExecutor(max_workers=threads) as ex:
         t0 = time.perf_counter()
         list(ex.map(one, idx))
         wall = time.perf_counter() - t0
-    rate = n_img / wall
+    return wall, threads, kind
+
+
+def cpu_reference_rate(wl, cpu_seconds, threads):
+    """images/s of the reference CPU op (fwd+bwd) on `threads` host threads,
+    over as many one-image-per-thread steps as fit in ~cpu_seconds."""
+    import oracle
+
+    use_ref = oracle.reference_available()
+    wall, imgs, kind = cpu_reference_step(wl, threads, use_ref)
+    steps = max(1, int(cpu_seconds / max(wall, 1e-3)) - 1)
+    tot, n = 0.0, 0
+    for _ in range(steps):
+        w, i, _ = cpu_reference_step(wl, threads, use_ref)
+        tot += w
+        n += i
+    rate = n / tot
     return {"value": rate, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{n_img} images of the {wl.name} layer ({wl.description}), fwd+bwd, one image per task on "
-                      f"{threads} threads; single-thread fwd {1.0 / tf1:.3g} img/s, fwd+bwd {1.0 / t1:.3g} img/s",
-            "fwd_value": threads / tf1 if tf1 > 0 else None, "seconds": wall}
+            "sample": f"{n} images of the {wl.name} layer ({wl.description}) in {steps} steps of {threads}, fwd+bwd, "
+                      f"one image per thread on {threads} threads ({tot:.1f} s)"}
 
 
 def run_reference_arm(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    from paraconv2d_b200 import workloads
+    import oracle
 
+    workloads = load_workloads()
     wl = workloads.WORKLOADS[args.workload]
+    if len(wl.layers) > 1:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference has no multi-layer or data-parallel path"}))
+        return 0
     cores = host_cores()
-    per_step = max(2.0, args.cpu_seconds / max(1, args.steps))
+    use_ref = oracle.reference_available()
     for _ in range(args.warmup):
-        pass  # the reference CPU op has no warm-up state worth timing
-    vals = []
-    last = None
+        cpu_reference_step(wl, cores, use_ref)
+    walls, imgs, kind = [], 0, None
     for _ in range(args.steps):
-        last = cpu_reference_rate(wl, per_step, cores)
-        vals.append(last["value"])
-    value = statistics.median(vals)
+        w, i, kind = cpu_reference_step(wl, cores, use_ref)
+        walls.append(w)
+        imgs += i
+    tot = sum(walls)
+    value = imgs / tot
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 0, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * wl.n / value, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": f"{wl.name}: {wl.description}", "per_gpu_batch": wl.n, "host_cores": cores},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": last["kind"], "sample": last["sample"]},
+        "impl": "reference", "metric": metric_of(wl), "value": value, "unit": UNIT, "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": layer_config(wl, wl.n, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": f"each step: forward + backward of {cores} images of the {wl.name} layer "
+                                   f"({wl.description}; images taken in turn from the seeded batch), one image per "
+                                   f"thread on {cores} host threads; {imgs} images in {tot:.1f} s"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
+def layer_config(wl, n, world):
+    """The `config` of the headline line (both arms)."""
+    return {"workload": f"{wl.name}: {wl.description}", "per_gpu_batch": n, "global_batch": n * world,
+            "parallelism": f"dp{world}" if world > 1 else "single GPU",
+            "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) before every step, outside the timed events",
+            "kernel_timing": "per-kernel CUDA events in a second pass of the same steps (off in the value pass)",
+            "precision": "fp32 via 3xTF32 tensor-core split where the tcgen05 kernels apply"}
+
+
 # ------------------------------------------------------------------ our arm
 
-def run_ours(args):
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        pg = dist
+def bench_layer(args, wl, lib, D, rank, world):
+    """The single-layer headline: device-resident steps through the C ABI,
+    per-kernel times, the end-to-end leg through the module."""
     import paraconv2d_b200 as pc
-    from paraconv2d_b200 import _lib, workloads
+    from paraconv2d_b200 import _lib
 
-    wl = workloads.WORKLOADS[args.workload]
+    workloads = load_workloads()
+    dev = D.dev
     L = wl.layer
-    lib = _lib.cabi()
     x, pars, g = workloads.draw(wl)
     grad = workloads.draw_grad(wl, g)
     xp = workloads.pad_input(x, L.p).to(dev)
@@ -311,37 +394,20 @@ def run_ours(args):
         if st != 0:
             raise RuntimeError(_lib.status_message(st))
 
-    def allreduce():
-        if pg is not None:
-            pg.all_reduce(dp)
-
-    def barrier():
-        if pg is not None:
-            pg.barrier()
-
-    def max_over_ranks(v):
-        if pg is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
-
-    # ---- device-resident steps, split into forward / backward events
     for _ in range(args.warmup):
         fwd()
         bwd()
-        allreduce()
+        D.all_reduce(dp)
     torch.cuda.synchronize()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
-    barrier()
+    D.barrier()
     torch.cuda.synchronize()
     # The headline pass runs with the library's per-kernel event timing off:
     # those events (two per kernel) cost ~20 us per step and sit between
     # dgrad and wgrad, which stops wgrad from starting on the SMs dgrad has
     # left.  A second pass of the same steps, with them on, gives the
     # per-kernel durations of the roofline.
-    clk = ClockSampler(local)
-    clk.__enter__()
+    clk = ClockSampler(D.dev.index).start()
     for i in range(args.steps):
         flush.zero_()
         ev[i][0].record(stream)
@@ -349,30 +415,28 @@ def run_ours(args):
         ev[i][1].record(stream)
         bwd()
         ev[i][2].record(stream)
-        allreduce()
+        D.all_reduce(dp)
         ev[i][3].record(stream)
     torch.cuda.synchronize()
-    barrier()
+    D.barrier()
     lib.pc2d_timing_reset()
     lib.pc2d_timing_enable(1)
     for i in range(args.steps):
         flush.zero_()
         fwd()
         bwd()
-        allreduce()
+        D.all_reduce(dp)
     torch.cuda.synchronize()
     lib.pc2d_timing_enable(0)
     ktimes = _lib.kernel_times(KERNELS)
-    barrier()
+    D.barrier()
     t_fwd = [e[0].elapsed_time(e[1]) / 1e3 for e in ev]
     t_bwd = [e[1].elapsed_time(e[2]) / 1e3 for e in ev]
     t_step = [e[0].elapsed_time(e[3]) / 1e3 for e in ev]
-    tot_step = max_over_ranks(sum(t_step))
-    tot_fwd = max_over_ranks(sum(t_fwd))
-    tot_bwd = max_over_ranks(sum(t_bwd))
+    tot_step = D.max(sum(t_step))
+    tot_fwd = D.max(sum(t_fwd))
+    tot_bwd = D.max(sum(t_bwd))
     images = n * world * args.steps
-    value = images / tot_step
-    fwd_value = images / tot_fwd
 
     # ---- end to end through the public module, host buffers
     layer = pc.ParaConv2d(L.cin, L.cout, L.k, stride=L.s, padding=L.p).to(dev)
@@ -380,14 +444,14 @@ def run_ours(args):
         layer.pars.copy_(p)
     x_host = x.pin_memory()
     g_host = grad.pin_memory()
+    out_host = torch.empty((n, m, P, Q), dtype=torch.float32).pin_memory()
+    dx_host = torch.empty(x.shape, dtype=torch.float32).pin_memory()
     dp_host = torch.empty(p.numel(), dtype=torch.float32).pin_memory()
-
     copy_stream = torch.cuda.Stream(dev)
 
     def e2e_step(start_event=None):
         # the upstream gradient crosses PCIe on a second stream, concurrently
-        # with the input copy and the forward; it starts after the step's
-        # start event, and the backward waits for it
+        # with the input copy and the forward; the backward waits for it
         if start_event is not None:
             copy_stream.wait_event(start_event)
         else:
@@ -397,22 +461,20 @@ def run_ours(args):
             g_ready = torch.cuda.Event()
             g_ready.record(copy_stream)
         gdd.record_stream(stream)
-        xd = x_host.to(dev, non_blocking=True)
+        xd = x_host.to(dev, non_blocking=True).requires_grad_(True)
         layer.pars.grad = None
         y = layer(xd)
+        out_host.copy_(y.detach(), non_blocking=True)
         stream.wait_event(g_ready)
         y.backward(gdd)
-        allreduce_e2e(layer.pars.grad)
+        D.all_reduce(layer.pars.grad)
+        dx_host.copy_(xd.grad, non_blocking=True)
         dp_host.copy_(layer.pars.grad, non_blocking=True)
-
-    def allreduce_e2e(t):
-        if pg is not None:
-            pg.all_reduce(t)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
     torch.cuda.synchronize()
-    barrier()
+    D.barrier()
     e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_tot = 0.0
     for _ in range(args.steps):
@@ -422,12 +484,12 @@ def run_ours(args):
         e_e.record(stream)
         e_e.synchronize()
         e_tot += e_s.elapsed_time(e_e) / 1e3
-    e_tot = max_over_ranks(e_tot)
-    clk.__exit__(None, None, None)
-    barrier()
+    e_tot = D.max(e_tot)
+    clk.stop()
+    D.barrier()
     e2e_value = images / e_tot
-    h2d = x_host.numel() * 4 + g_host.numel() * 4
-    d2h = dp_host.numel() * 4
+    h2d = (x_host.numel() + g_host.numel()) * 4
+    d2h = (out_host.numel() + dx_host.numel() + dp_host.numel()) * 4
 
     # ---- roofline of the dominant kernel (per-launch CUDA-event times of
     # the second timed pass; each main kernel does 4*m*d*n*P*Q algorithmic
@@ -435,8 +497,6 @@ def run_ours(args):
     peaks = measured_peaks()
     tf32 = measure_tf32_tflops(dev)
     peak_3x = tf32 / 3.0
-    f_fwd = workloads.fwd_flops_per_image(wl) * n
-    f_bwd = workloads.bwd_flops_per_image(wl) * n
     mean_fwd = tot_fwd / args.steps
     mean_bwd = tot_bwd / args.steps
     timed = {k: v for k, v in ktimes.items() if v[1] > 0}
@@ -444,53 +504,31 @@ def run_ours(args):
     dom_ms = timed[dom][0] / timed[dom][1] if timed else 1e3 * mean_fwd
     kflops = workloads.fwd_flops_per_image(wl) * n  # forward, dgrad and wgrad kernels alike
     achieved = kflops / (dom_ms / 1e3) / 1e12
-    fwd_frac = f_fwd / mean_fwd / 1e12 / peak_3x
-    bwd_frac = f_bwd / mean_bwd / 1e12 / peak_3x
-    tr = NCU_TRAFFIC_BYTES.get((args.workload, dom))
+    tr = NCU_TRAFFIC_BYTES.get((wl.name, dom))
+    bf16_burst = peaks.get("bf16_tflops")
     roofline = {
         "bound": "tensor", "achieved": achieved, "peak": peak_3x, "unit": "TFLOP/s", "frac": achieved / peak_3x,
-        "traffic": tr, "kernel": dom, "kernel_ms": dom_ms,
+        "traffic": tr, "traffic_source": TRAFFIC_SOURCE if tr else None, "kernel": dom, "kernel_ms": dom_ms,
+        "algorithmic_flops_per_launch": kflops,
         "kernel_ms_all": {k: v[0] / v[1] for k, v in timed.items()},
         "peak_source": f"measured TF32 cuBLAS GEMM {tf32:.0f} TFLOP/s on this GPU / 3 (3xTF32 issues three MMAs per "
-                       f"algorithmic multiply-add); bf16 dense {peaks.get('bf16_tflops')} TFLOP/s of measured "
-                       f"(MEASURED_PEAKS.json)",
-        "fwd_frac": fwd_frac, "bwd_frac": bwd_frac,
+                       f"algorithmic multiply-add); bf16 dense {bf16_burst} TFLOP/s of measured (MEASURED_PEAKS.json)",
+        "frac_of_bf16_half": (achieved / (bf16_burst / 6.0)) if bf16_burst else None,
+        "fwd_frac": workloads.fwd_flops_per_image(wl) * n / mean_fwd / 1e12 / peak_3x,
+        "bwd_frac": workloads.bwd_flops_per_image(wl) * n / mean_bwd / 1e12 / peak_3x,
         "hbm_gbs_fwd": workloads.fwd_bytes_per_image(wl) * n / mean_fwd / 1e9,
         "hbm_peak_gbs": peaks.get("hbm_gbs"),
     }
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            cb = cpu_reference_rate(wl, args.cpu_seconds, host_cores())
-            cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
-        except Exception as exc:  # the baseline is reported, never required
-            cpu = {"value": None, "unit": UNIT, "cores": host_cores(), "kind": "port", "sample": f"failed: {exc}"}
-
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 * tot_step / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-            "config": {"workload": f"{wl.name}: {wl.description}", "per_gpu_batch": n, "global_batch": n * world,
-                       "parallelism": f"dp{world}" if world > 1 else "single GPU",
-                       "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) before every step, outside the timed events",
-                       "kernel_timing": "per-kernel CUDA events in a second pass of the same steps (off in the value pass)",
-                       "precision": "fp32 via 3xTF32 tensor-core split where the tcgen05 kernels apply",
-                       "algo": {0: "auto", 1: "simt", 2: "tc"}[lib.pc2d_get_algo()]},
-            "fwd_images_per_s": fwd_value, "fwd_ms": 1e3 * mean_fwd, "bwd_ms": 1e3 * mean_bwd,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * launches_per_step(lib, ktimes, args.steps),
-            "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
-    if pg is not None:
-        pg.barrier()
-        pg.destroy_process_group()
-    return 0
+    return {
+        "value": images / tot_step, "ms_per_step": 1e3 * tot_step / args.steps,
+        "fwd_images_per_s": images / tot_fwd, "fwd_ms": 1e3 * mean_fwd, "bwd_ms": 1e3 * mean_bwd,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps * launches_per_step(ktimes, args.steps),
+        "roofline": roofline, "clock": clk, "algo": {0: "auto", 1: "simt", 2: "tc"}[lib.pc2d_get_algo()],
+    }
 
 
-def launches_per_step(lib, ktimes, steps):
+def launches_per_step(ktimes, steps):
     """Our kernel launches per device-resident step, from the timed main
     kernels: tcgen05 forward = 1 prep kernel + the main kernel; tcgen05
     dgrad = 1 prep + main; tcgen05 wgrad = main + fixed-order reduction;
@@ -500,126 +538,198 @@ def launches_per_step(lib, ktimes, steps):
     return total // max(1, steps)
 
 
-def run_stack(args):
-    """Data-parallel training step of a multi-layer stack (the c5 workload:
-    3->32->64->64->64, k3 p1, stride 2 on layers 2-3, 64x64 input, global batch
-    1024, loss = sum(out^2)).  The global batch is split across the ranks
-    (strong scaling); one bucketed NCCL all-reduce (SUM) of all parameter
-    gradients per step."""
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        pg = dist
+def bench_stack(args, wl, lib, D, rank, world, steps):
+    """Data-parallel training step of the layer stack (the c5 workload:
+    3->32->64->64->64, k3 p1, stride 2 on layers 2-3, 64x64 input, global
+    batch 1024, loss sum((2^-40 out)^2)).  The global batch is split across
+    the ranks (strong scaling); each layer's parameter gradient is summed
+    across the ranks by an asynchronous NCCL all-reduce issued as soon as it
+    is accumulated, overlapping the backward of the layers below it."""
     import paraconv2d_b200 as pc
-    from paraconv2d_b200 import _lib, workloads
+    from paraconv2d_b200 import _lib
     from paraconv2d_b200.dp import GradAllReduce, shard
 
-    wl = workloads.WORKLOADS[args.workload]
-    lib = _lib.cabi()
+    workloads = load_workloads()
+    dev = D.dev
     x, pars, _ = workloads.draw(wl)
     xs = shard(x, rank, world).contiguous()
-    layers = []
-    for i, (L, pr) in enumerate(zip(wl.layers, pars)):
-        # the first layer's input needs no gradient: skip_input_grad, as the
-        # reference module documents for the first layer of a network
-        m = pc.ParaConv2d(L.cin, L.cout, L.k, stride=L.s, padding=L.p, skip_input_grad=(i == 0)).to(dev)
-        with torch.no_grad():
-            m.pars.copy_(pr.to(dev))
-        layers.append(m)
-    model = torch.nn.Sequential(*layers)
-    reducer = GradAllReduce(model.parameters()) if world > 1 else None
+
+    def make_model():
+        mods = []
+        for i, (L, pr) in enumerate(zip(wl.layers, pars)):
+            # the first layer's input needs no gradient: skip_input_grad, as
+            # the reference module documents for the first layer of a network
+            m = pc.ParaConv2d(L.cin, L.cout, L.k, stride=L.s, padding=L.p, skip_input_grad=(i == 0)).to(dev)
+            with torch.no_grad():
+                m.pars.copy_(pr.to(dev))
+            mods.append(m)
+        return torch.nn.Sequential(*mods)
+
+    model = make_model()
+    params = list(model.parameters())
+    reducer = GradAllReduce(params, bucketed=False) if world > 1 else None
     xd = xs.to(dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def step(inp):
-        for prm in model.parameters():
+        for prm in params:
             prm.grad = None
-        y = model(inp)
-        (y * y).sum().backward()
+        loss = workloads.stack_loss(model(inp))
+        loss.backward()
         if reducer is not None:
             reducer()
-
-    def max_over_ranks(v):
-        if pg is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
+        return loss
 
     for _ in range(args.warmup):
         step(xd)
     torch.cuda.synchronize()
-    if pg is not None:
-        pg.barrier()
-    clk = ClockSampler(local)
-    clk.__enter__()
+    D.barrier()
     tot = 0.0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for _ in range(args.steps):
+    for _ in range(steps):
         flush.zero_()
         e0.record(stream)
         step(xd)
         e1.record(stream)
         e1.synchronize()
         tot += e0.elapsed_time(e1) / 1e3
+    tot = D.max(tot)
     # per-kernel durations from a second pass with the library's event timing
-    # on (kept out of the headline pass, as in run_layer)
+    # on (kept out of the headline pass, as in the layer bench)
+    D.barrier()
     lib.pc2d_timing_reset()
     lib.pc2d_timing_enable(1)
-    for _ in range(args.steps):
+    for _ in range(steps):
         flush.zero_()
         step(xd)
     torch.cuda.synchronize()
     lib.pc2d_timing_enable(0)
     ktimes = _lib.kernel_times(KERNELS)
-    tot = max_over_ranks(tot)
-    # end to end: the shard's input from pinned host memory, gradients read back
+    # end to end: the shard's input from pinned host memory; the loss and the
+    # summed gradients read back
     x_host = xs.pin_memory()
-    grads_host = [torch.empty(prm.numel()).pin_memory() for prm in model.parameters()]
+    grads_host = [torch.empty(prm.numel()).pin_memory() for prm in params]
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    D.barrier()
     e_tot = 0.0
-    for _ in range(args.steps):
+    for _ in range(steps):
         flush.zero_()
         e0.record(stream)
-        step(x_host.to(dev, non_blocking=True))
-        for gh, prm in zip(grads_host, model.parameters()):
+        loss = step(x_host.to(dev, non_blocking=True))
+        loss_host.copy_(loss.detach(), non_blocking=True)
+        for gh, prm in zip(grads_host, params):
             gh.copy_(prm.grad, non_blocking=True)
         e1.record(stream)
         e1.synchronize()
         e_tot += e0.elapsed_time(e1) / 1e3
-    e_tot = max_over_ranks(e_tot)
-    clk.__exit__(None, None, None)
-    images = wl.n * args.steps
-    flops_img = sum((2 if i == 0 else 3) * workloads.fwd_flops_per_image(wl, i) for i in range(len(wl.layers)))
-    peak_3x = measure_tf32_tflops(dev) / 3.0
+    e_tot = D.max(e_tot)
+    # the all-reduce on its own: one flat bucket of all gradients, blocking
+    ar_ms = None
+    if world > 1:
+        flat = torch.cat([prm.grad.reshape(-1) for prm in params])
+        for _ in range(3):
+            D.all_reduce(flat)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(steps):
+            D.all_reduce(flat)
+        a1.record(stream)
+        a1.synchronize()
+        ar_ms = D.max(a0.elapsed_time(a1) / steps)
+    # data-parallel parity: the all-reduced gradients of the last step
+    # against the gradient of the whole batch in one process (rank 0)
+    got = [prm.grad.detach().clone() for prm in params]
+    parity = None
+    D.barrier()
     if rank == 0:
-        timed = {k: v for k, v in ktimes.items() if v[1] > 0}
+        ref_model = make_model()
+        workloads.stack_loss(ref_model(x.to(dev))).backward()
+        errs = []
+        for a, prm in zip(got, ref_model.parameters()):
+            b = prm.grad.detach()
+            errs.append(float((a - b).abs().max() / b.abs().max().clamp_min(1e-300)))
+        finite = all(bool(torch.isfinite(a).all()) for a in got)
+        parity = {"max_rel_err_per_layer": errs, "tolerance": 1e-4, "finite": finite,
+                  "pass": finite and max(errs) <= 1e-4,
+                  "what": "max|allreduced - one-process full-batch| / max|full-batch| per layer's pars.grad"}
+        del ref_model
+    D.barrier()
+    peak_3x = None
+    if rank == 0:
+        peak_3x = measure_tf32_tflops(dev) / 3.0
+    images = wl.n * steps
+    flops_img = sum((2 if i == 0 else 3) * workloads.fwd_flops_per_image(wl, i) for i in range(len(wl.layers)))
+    timed = {k: v for k, v in ktimes.items() if v[1] > 0}
+    res = {
+        "metric": metric_of(wl), "value": images / tot, "unit": UNIT, "n_gpus": world, "steps": steps,
+        "ms_per_step": 1e3 * tot / steps, "scaling": "strong", "global_batch": wl.n, "per_gpu_batch": int(xs.shape[0]),
+        "allreduce": "one async NCCL all-reduce (SUM) per layer, issued from its post-accumulate-grad hook"
+                     if world > 1 else None,
+        "allreduce_ms_flat_bucket": ar_ms,
+        "e2e": {"value": images / e_tot, "unit": UNIT, "h2d_bytes_per_step": x_host.numel() * 4,
+                "d2h_bytes_per_step": sum(g.numel() * 4 for g in grads_host) + 4},
+        "kernel_ms_per_step": {k: v[0] / steps for k, v in timed.items()},
+        "dp_parity": parity,
+    }
+    if peak_3x:
+        res["tensor_frac_of_step"] = flops_img * wl.n / (tot / steps) / 1e12 / peak_3x / world
+    if reducer is not None:
+        reducer.remove()
+    return res
+
+
+def run_ours(args):
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    D = Dist(world, dev)
+    from paraconv2d_b200 import _lib
+
+    workloads = load_workloads()
+    lib = _lib.cabi()
+    wl = workloads.WORKLOADS[args.workload]
+    if len(wl.layers) > 1:
+        clk = ClockSampler(local).start()
+        res = bench_stack(args, wl, lib, D, rank, world, args.steps)
+        clk.stop()
+        if rank == 0:
+            line = dict(res)
+            line.update({"warmup": args.warmup, "higher_is_better": True, "vs_baseline": None, "dtype": "f32",
+                         "data": "synthetic (seeded)",
+                         "config": {"workload": f"{wl.name}: {wl.description}", "global_batch": wl.n,
+                                    "per_gpu_batch": res["per_gpu_batch"], "parallelism": f"dp{world}"},
+                         "clocks": clk.summary()})
+            print(json.dumps(line), flush=True)
+        D.close()
+        return 0
+
+    r = bench_layer(args, wl, lib, D, rank, world)
+    stack = None
+    if not args.no_stack:
+        clk_s = ClockSampler(local).start()
+        stack = bench_stack(args, workloads.WORKLOADS[STACK], lib, D, rank, world, args.stack_steps)
+        clk_s.stop()
+        stack["clocks"] = clk_s.summary()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_reference_rate(wl, args.cpu_seconds, host_cores())
+        except Exception as exc:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": UNIT, "cores": host_cores(), "kind": "port", "sample": f"failed: {exc}"}
+    if rank == 0:
+        cfg = layer_config(wl, wl.n, world)
         line = {
-            "metric": f"{wl.name} data-parallel training step images/s", "value": images / tot, "unit": UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded)",
-            "config": {"workload": f"{wl.name}: {wl.description}", "global_batch": wl.n,
-                       "per_gpu_batch": xs.shape[0], "parallelism": f"dp{world}",
-                       "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) before every step, outside the timed events",
-                       "kernel_timing": "per-kernel CUDA events in a second pass of the same steps (off in the value pass)"},
-            "e2e": {"value": images / e_tot, "unit": UNIT, "h2d_bytes_per_step": x_host.numel() * 4,
-                    "d2h_bytes_per_step": sum(g.numel() * 4 for g in grads_host)},
-            "tensor_frac_of_step": flops_img * wl.n / (tot / args.steps) / 1e12 / peak_3x / world,
-            "kernel_ms_per_step": {k: v[0] / args.steps for k, v in timed.items()},
-            "clocks": clk.summary(),
+            "metric": metric_of(wl), "value": r["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "config": cfg,
+            "fwd_images_per_s": r["fwd_images_per_s"], "fwd_ms": r["fwd_ms"], "bwd_ms": r["bwd_ms"],
+            "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "roofline": r["roofline"], "cpu_baseline": cpu,
+            "clocks": r["clock"].summary(), "algo": r["algo"], "dp_step": stack,
         }
         print(json.dumps(line), flush=True)
-    if pg is not None:
-        pg.barrier()
-        pg.destroy_process_group()
+    D.close()
     return 0
 
 
@@ -627,9 +737,6 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
-    from paraconv2d_b200 import workloads
-    if len(workloads.WORKLOADS[args.workload].layers) > 1:
-        return run_stack(args)
     return run_ours(args)
 
 

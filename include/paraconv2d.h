@@ -99,11 +99,12 @@ int pc2d_forward(int dtype, const void *input, const void *pars, double factor,
  * a fixed memory budget: cudaMalloc can synchronise the device or fail, and
  * those hosts forbid it.  The scratch lives in a static 8 MiB device array
  * that every GPU loading the library keeps until exit.  Problems needing more
- * scratch than that fail with PC2D_ERR_WORKSPACE.  The first call on a device
- * resolves the array's address with cudaGetSymbolAddress, so make that first
- * call before any stream capture.  All calls share the array: calls that
- * overlap on the GPU race and must be serialised by the caller.  Arguments,
- * results and the other errors are those of pc2d_forward. */
+ * scratch than that fail with PC2D_ERR_WORKSPACE.  The first call in each
+ * CUDA context (with a device's primary context current: the first call on
+ * that device) resolves the array's address with cudaGetSymbolAddress, so
+ * make that first call before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race and must be serialised by the
+ * caller.  Arguments, results and the other errors are those of pc2d_forward. */
 int pc2d_forward_noalloc(int dtype, const void *input, const void *pars, double factor,
                          int k0, int k1, int s0, int s1, int dl0, int dl1,
                          int n, int channels, int height, int width, int m,

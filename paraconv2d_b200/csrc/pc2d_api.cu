@@ -9,6 +9,8 @@
 #include <mutex>
 #include <vector>
 
+#include <cuda.h>  // CUcontext, CUresult (types only; entry points resolved at run time)
+
 #include "pc2d_common.cuh"
 #include "pc2d_tc.cuh"
 
@@ -45,9 +47,43 @@ cudaEvent_t timing_event() {
   return e;
 }
 std::atomic<int> g_algo{PC2D_ALGO_AUTO};
-std::mutex g_status_mutex;
-int *g_status_ptrs[64] = {nullptr};
+PerContext<int *> g_status_ptrs;
+
+// cuCtxGetCurrent and cuCtxGetId, resolved once through the runtime (the
+// library links the CUDA runtime only).
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+struct CtxFns {
+  CtxGetCurrentFn get_current = nullptr;
+  CtxGetIdFn get_id = nullptr;
+};
+const CtxFns &ctx_fns() {
+  static CtxFns fns;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fns.get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fns.get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  return fns;
+}
 }  // namespace
+
+unsigned long long current_context_id() {
+  const CtxFns &f = ctx_fns();
+  if (!f.get_current || !f.get_id) return 0;
+  CUcontext ctx = nullptr;
+  if (f.get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (f.get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 void set_last_error(const char *fmt, ...) {
   va_list ap;
@@ -72,15 +108,15 @@ void timing_end(KernelId id, cudaStream_t stream) {
 }
 
 int *device_status_ptr() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(g_status_mutex);
-  if (g_status_ptrs[dev] == nullptr) {
-    void *ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_device_status) != cudaSuccess) return nullptr;
-    g_status_ptrs[dev] = reinterpret_cast<int *>(ptr);
-  }
-  return g_status_ptrs[dev];
+  unsigned long long ctx = current_context_id();
+  int *cached = nullptr;
+  if (ctx && g_status_ptrs.get(ctx, &cached)) return cached;
+  void *ptr = nullptr;
+  if (cudaGetSymbolAddress(&ptr, g_device_status) != cudaSuccess) return nullptr;
+  // the lookup may have made the device's primary context current
+  if (!ctx) ctx = current_context_id();
+  if (ctx) g_status_ptrs.set(ctx, reinterpret_cast<int *>(ptr));
+  return reinterpret_cast<int *>(ptr);
 }
 
 namespace {

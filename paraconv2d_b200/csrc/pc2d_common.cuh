@@ -5,9 +5,68 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <utility>
+#include <vector>
+
 #include "paraconv2d.h"
 
 namespace pc2d {
+
+// Unique id (cuCtxGetId) of the CUDA context current on the calling thread;
+// 0 when no context is current or the driver cannot say.  Ids are never
+// reused within a process, unlike context handles or device ordinals.
+unsigned long long current_context_id();
+
+// Values kept per CUDA context.  Device addresses of this library's
+// __device__ variables and per-kernel attributes belong to the module loaded
+// into one context; a host may make a context other than the device's
+// primary one current, so caches are keyed on the context, not the device.
+template <typename T>
+class PerContext {
+ public:
+  bool get(unsigned long long id, T *v) {
+    std::lock_guard<std::mutex> lock(mu_);
+    for (auto &e : entries_)
+      if (e.first == id) {
+        *v = e.second;
+        return true;
+      }
+    return false;
+  }
+  void set(unsigned long long id, T v) {
+    std::lock_guard<std::mutex> lock(mu_);
+    for (auto &e : entries_)
+      if (e.first == id) {
+        e.second = v;
+        return;
+      }
+    entries_.emplace_back(id, v);
+  }
+
+ private:
+  std::mutex mu_;
+  std::vector<std::pair<unsigned long long, T>> entries_;
+};
+
+// Runs `fn` (a function returning a pc2d_status) once per context for each
+// bit of `cache`: a cudaFuncSetAttribute call, typically.  Without a context
+// id it runs every time.
+template <typename F>
+int once_per_context(PerContext<uint64_t> &cache, uint64_t bit, F &&fn) {
+  unsigned long long ctx = current_context_id();
+  uint64_t mask = 0;
+  if (ctx && cache.get(ctx, &mask) && (mask & bit)) return PC2D_OK;
+  const int st = fn();
+  if (st != PC2D_OK) return st;
+  if (!ctx) ctx = current_context_id();
+  if (ctx) {
+    mask = 0;
+    cache.get(ctx, &mask);
+    cache.set(ctx, mask | bit);
+  }
+  return PC2D_OK;
+}
 
 // One ParaConv2d problem (a padded input batch and one parameter vector).
 // Field names follow the reference op (paraconv2d.cc:254-269).
@@ -48,7 +107,7 @@ __host__ __device__ inline int tap_col(const Problem &p, int tap) { return (p.k1
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Device-side status word of the current device: the first nonzero
+// Device-side status word of the current context: the first nonzero
 // pc2d_status a kernel records (a bounded mbarrier wait that gave up).  It is
 // a __device__ variable of the ABI translation unit; kernels get its address
 // as an argument.  Read by pc2d_device_status().

@@ -17,17 +17,18 @@
 // Rules of use:
 //   - problems whose scratch would exceed kNoAllocScratchBytes are rejected
 //     with PC2D_ERR_WORKSPACE before anything is launched;
-//   - the first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (with that device current).  That lookup allocates
+//   - the first call in a CUDA context (on a device's primary context: the
+//     first call on that device) looks up the array's device address with
+//     cudaGetSymbolAddress, with that context current.  That lookup allocates
 //     nothing but may load the module; make the first call on each device
-//     before any stream capture;
+//     (and in each other context a host creates) before any stream capture.
+//     The address is cached per context, because a module's addresses belong
+//     to the context it was loaded into;
 //   - all calls share the one array, which keeps the previous call's contents.
 //     Nothing has to start at zero: the forward's prep kernels overwrite every
 //     scratch byte it reads.  Calls that overlap on the GPU (different streams,
 //     or different host threads, on one device) race on the array and must be
 //     serialised by the caller.
-#include <mutex>
-
 #include "pc2d_common.cuh"
 
 namespace pc2d {
@@ -37,30 +38,23 @@ constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // 8 MiB
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_noalloc_mutex;
-void *g_noalloc_ptr[64] = {nullptr};
+PerContext<void *> g_noalloc_ptr;
 
-// Device address of g_noalloc_scratch on the current device (looked up once
-// per device); nullptr with a message on failure.
+// Device address of g_noalloc_scratch in the current context (looked up once
+// per context); nullptr with a message on failure.
 void *noalloc_scratch_ptr() {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    set_last_error("pc2d_forward_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+  unsigned long long ctx = current_context_id();
+  void *ptr = nullptr;
+  if (ctx && g_noalloc_ptr.get(ctx, &ptr)) return ptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess || ptr == nullptr) {
+    set_last_error("pc2d_forward_noalloc: cudaGetSymbolAddress of the scratch array failed (%s)", cudaGetErrorString(e));
     return nullptr;
   }
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void *ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || ptr == nullptr) {
-      set_last_error("pc2d_forward_noalloc: cudaGetSymbolAddress of the scratch array failed on device %d (%s)", dev,
-                     cudaGetErrorString(e));
-      return nullptr;
-    }
-    g_noalloc_ptr[dev] = ptr;
-  }
-  return g_noalloc_ptr[dev];
+  // the lookup may have made the device's primary context current
+  if (!ctx) ctx = current_context_id();
+  if (ctx) g_noalloc_ptr.set(ctx, ptr);
+  return ptr;
 }
 
 }  // namespace
@@ -71,7 +65,10 @@ extern "C" int pc2d_forward_noalloc(int dtype, const void *input, const void *pa
                                     int m, void *output, void *hsum, void *stream) {
   using namespace pc2d;
   // Shape checks and the scratch size come from the regular entry points, so a
-  // problem this call accepts is exactly one pc2d_forward accepts.
+  // problem this call accepts is exactly one pc2d_forward accepts.  The size
+  // check here gives a clear message; pc2d_forward checks again against the
+  // kernel path it actually takes (the process-wide kernel family may change
+  // between the two).
   const size_t need = pc2d_forward_workspace_size(dtype, n, channels, height, width, m, k0, k1, s0, s1, dl0, dl1);
   if (need > kNoAllocScratchBytes) {
     set_last_error("pc2d_forward_noalloc: this problem needs %zu bytes of scratch, more than the %zu-byte static "
@@ -79,11 +76,8 @@ extern "C" int pc2d_forward_noalloc(int dtype, const void *input, const void *pa
                    need, kNoAllocScratchBytes);
     return PC2D_ERR_WORKSPACE;
   }
-  void *ws = nullptr;
-  if (need > 0) {
-    ws = noalloc_scratch_ptr();
-    if (ws == nullptr) return PC2D_ERR_CUDA;
-  }
+  void *ws = noalloc_scratch_ptr();
+  if (ws == nullptr) return PC2D_ERR_CUDA;
   return pc2d_forward(dtype, input, pars, factor, k0, k1, s0, s1, dl0, dl1, n, channels, height, width, m, output,
-                      hsum, ws, need, stream);
+                      hsum, ws, kNoAllocScratchBytes, stream);
 }

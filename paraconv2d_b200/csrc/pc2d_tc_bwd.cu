@@ -669,21 +669,16 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   }
 }
 
-std::mutex g_attr_mutex;
-bool g_attr_set[64][4] = {};
+PerContext<uint64_t> g_attr;
 
 template <int NC>
 int launch_dgrad(const Problem &p, DgCfg c, const float *grad, const float *x, const float *hsum,
                  const float *wsB, float *dx, int *status, cudaStream_t stream) {
-  int dev = 0;
-  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
-  {
-    std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (dev >= 0 && dev < 64 && !g_attr_set[dev][NC / 16 - 1]) {
-      PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_dgrad_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-      g_attr_set[dev][NC / 16 - 1] = true;
-    }
-  }
+  const int ast = once_per_context(g_attr, 1ull << (NC / 16 - 1), []() -> int {
+    PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_dgrad_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    return (int)PC2D_OK;
+  });
+  if (ast != PC2D_OK) return ast;
   CUtensorMap gmap, hmap;
   std::memset(&gmap, 0, sizeof(gmap));
   std::memset(&hmap, 0, sizeof(hmap));

@@ -517,8 +517,7 @@ __global__ void __launch_bounds__(kColThreads) tc_dc_col2im(const float *__restr
   }
 }
 
-std::mutex g_attr_mutex;
-bool g_attr_set[64][kMaxNP / 16] = {};
+PerContext<uint64_t> g_attr;
 
 template <int NP>
 int launch_dc_gemm(const Problem &p, DcCfg c, const float *grad, const float *hsum, const float *wsB, float *Y,
@@ -530,16 +529,12 @@ int launch_dc_gemm(const Problem &p, DcCfg c, const float *grad, const float *hs
   if (c.tma && !(encode_planes_map(grad, p.PQ, (int64_t)p.n * p.m, kTileM, 16, &gmap) &&
                  encode_planes_map(hsum, p.PQ, (int64_t)p.n * p.m, kTileM, 16, &hmap)))
     c.tma = 0;  // direct global loads instead
-  int dev = 0;
-  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
-  {
-    std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (dev >= 0 && dev < 64 && !g_attr_set[dev][NP / 16 - 1]) {
-      PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_dc_gemm_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kSmemLimit));
-      g_attr_set[dev][NP / 16 - 1] = true;
-    }
-  }
+  const int ast = once_per_context(g_attr, 1ull << (NP / 16 - 1), []() -> int {
+    PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_dc_gemm_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemLimit));
+    return (int)PC2D_OK;
+  });
+  if (ast != PC2D_OK) return ast;
   const int grid = (int)std::min<int64_t>(c.tiles, device_sm_count());
   tc_dc_gemm_kernel<NP><<<grid, kThreads, dc_smem_bytes(c), stream>>>(grad, hsum, wsB, p, c, gmap, hmap, Y, status);
   PC2D_LAUNCH_CHECK("tc_dc_gemm_kernel");

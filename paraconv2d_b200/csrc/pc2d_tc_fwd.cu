@@ -629,25 +629,20 @@ __global__ void selftest_wait_kernel(unsigned int timeout_us, int *status) {
     record_device_error(status, PC2D_ERR_TIMEOUT);
 }
 
-std::mutex g_attr_mutex;
-bool g_attr_set[64][8] = {};
+PerContext<uint64_t> g_attr;
+std::mutex g_sm_mutex;
 int g_sm_count[64] = {0};
 
 template <int NB, int SUB>
 int launch_forward_sub(const Problem &p, const FwdCfg &c, const CUtensorMap &xmap, const float *x, const float *pars,
                        const float *wsB, const float *cj, float factor, float *out, float *hsum, int *status,
                        cudaStream_t stream) {
-  int dev = 0;
-  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
-  {
-    std::lock_guard<std::mutex> lock(g_attr_mutex);
-    const int slot = (NB / 16 - 1) * 2 + (SUB - 1);
-    if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot]) {
-      PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_forward_kernel<NB, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           227 * 1024));
-      g_attr_set[dev][slot] = true;
-    }
-  }
+  const int ast = once_per_context(g_attr, 1ull << ((NB / 16 - 1) * 2 + (SUB - 1)), []() -> int {
+    PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_forward_kernel<NB, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024));
+    return (int)PC2D_OK;
+  });
+  if (ast != PC2D_OK) return ast;
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
   timing_begin(K_FORWARD, stream);
   tc_forward_kernel<NB, SUB><<<grid, kFwdThreads, fwd_smem_bytes(p, c), stream>>>(x, pars, wsB, cj, factor, p, c, xmap,
@@ -721,7 +716,7 @@ bool encode_rows_map_sw128(const float *t, int64_t cols, int64_t rows, int box_r
 int device_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  std::lock_guard<std::mutex> lock(g_sm_mutex);
   if (g_sm_count[dev] == 0) {
     int v = 0;
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;

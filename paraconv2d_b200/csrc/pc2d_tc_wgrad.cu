@@ -785,14 +785,13 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
   }
 }
 
-std::mutex g_attr_mutex;
-bool g_attr_set[64] = {};
+PerContext<uint64_t> g_attr;
 
 }  // namespace
 
 bool tc_wgrad_supported(const Problem &p) {
   if (p.NPQ <= 0 || p.m < 1 || p.CHW >= ((int64_t)1 << 31) || p.PQ >= ((int64_t)1 << 30)) return false;
-  const WgCfg c = wg_cfg(p, 148);
+  const WgCfg c = wg_cfg(p, device_sm_count());
   return wg_smem_bytes(c) <= (size_t)kSmemLimit && c.NR <= 256 && 2 * c.JM <= 128;
 }
 
@@ -824,20 +823,16 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   }
   float *part = reinterpret_cast<float *>(ws);
   float *sums = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + wg_part_bytes(c));
-  int dev = 0;
-  PC2D_CUDA_CHECK(cudaGetDevice(&dev));
-  {
-    std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (dev >= 0 && dev < 64 && !g_attr_set[dev]) {
-      PC2D_CUDA_CHECK(
-          cudaFuncSetAttribute(tc_wgrad_kernel<false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-      PC2D_CUDA_CHECK(
-          cudaFuncSetAttribute(tc_wgrad_kernel<true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-      PC2D_CUDA_CHECK(
-          cudaFuncSetAttribute(tc_wgrad_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-      g_attr_set[dev] = true;
-    }
-  }
+  const int ast = once_per_context(g_attr, 1, []() -> int {
+    PC2D_CUDA_CHECK(
+        cudaFuncSetAttribute(tc_wgrad_kernel<false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    PC2D_CUDA_CHECK(
+        cudaFuncSetAttribute(tc_wgrad_kernel<true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    PC2D_CUDA_CHECK(
+        cudaFuncSetAttribute(tc_wgrad_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    return (int)PC2D_OK;
+  });
+  if (ast != PC2D_OK) return ast;
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
   timing_begin(K_WGRAD, stream);
   // Programmatic dependent launch: when the input-gradient kernel precedes

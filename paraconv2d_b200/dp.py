@@ -32,11 +32,15 @@ class GradAllReduce:
     """Sums the gradients of `params` across the ranks of `group`.
 
     ``bucketed=True`` (default) flattens all gradients into one buffer and
-    issues a single all-reduce per step: for a 4-layer 3->32->64->64->64 stack
-    that is 186,496 floats, far below the size where splitting pays on
-    NVLink.  ``bucketed=False`` issues one asynchronous all-reduce per
-    parameter as soon as its gradient is accumulated (overlapping the
-    remaining backward); ``wait()`` completes them."""
+    issues a single all-reduce after the backward: for a 4-layer
+    3->32->64->64->64 stack that is 186,496 floats.  The buffer always spans
+    every parameter (a parameter without a gradient on this rank contributes
+    zeros and receives the others' sum), so every rank issues a collective of
+    the same length.  ``bucketed=False`` issues one asynchronous all-reduce
+    per parameter as soon as its gradient is accumulated, overlapping the
+    backward of the layers below it; ``wait()`` completes them.  In that mode
+    every parameter must receive a gradient on every rank in every step (the
+    ranks must issue the same collectives in the same order)."""
 
     def __init__(self, params: Iterable[torch.nn.Parameter], group: Optional[dist.ProcessGroup] = None,
                  bucketed: bool = True):
@@ -58,26 +62,38 @@ class GradAllReduce:
         if not self.bucketed:
             self.wait()
             return
-        grads = [p.grad for p in self.params if p.grad is not None]
-        if not grads:
+        if not self.params:
             return
-        total = sum(g.numel() for g in grads)
-        if self._flat is None or self._flat.numel() != total or self._flat.device != grads[0].device:
-            self._flat = torch.empty(total, dtype=grads[0].dtype, device=grads[0].device)
+        ref = self.params[0]
+        total = sum(p.numel() for p in self.params)
+        if self._flat is None or self._flat.numel() != total or self._flat.device != ref.device:
+            self._flat = torch.empty(total, dtype=ref.dtype, device=ref.device)
         off = 0
-        for g in grads:
-            self._flat[off:off + g.numel()].copy_(g.reshape(-1))
-            off += g.numel()
+        for p in self.params:
+            seg = self._flat[off:off + p.numel()]
+            if p.grad is None:
+                seg.zero_()
+            else:
+                seg.copy_(p.grad.reshape(-1))
+            off += p.numel()
         dist.all_reduce(self._flat, op=dist.ReduceOp.SUM, group=self.group)
         off = 0
-        for g in grads:
-            g.copy_(self._flat[off:off + g.numel()].view_as(g))
-            off += g.numel()
+        for p in self.params:
+            seg = self._flat[off:off + p.numel()].view_as(p)
+            if p.grad is None:
+                p.grad = seg.clone()
+            else:
+                p.grad.copy_(seg)
+            off += p.numel()
 
     def wait(self):
+        n = len(self._works)
         for w in self._works:
             w.wait()
         self._works.clear()
+        if n != len(self.params):
+            raise RuntimeError(f"GradAllReduce: {n} of {len(self.params)} parameters received a gradient this step; "
+                               "per-parameter all-reduce needs every parameter's gradient on every rank")
 
     def remove(self):
         for h in self._hooks:

@@ -7,7 +7,8 @@ The five cases are the layer shapes the op is measured and checked on:
 * ``c3``: N=64, 64->128, 56x56, k3 s1 p1; |N(0,1)| input, N(0, 0.05^2), seed 2
 * ``c4``: N=32, 3->64, 224x224, k7 s2 p3; U(-1,1), N(0, 0.1^2), seed 3
 * ``c5``: a 4-layer stack 3->32->64->64->64, k3 p1, stride 2 on layers 2 and 3,
-  64x64 input, global batch 1024, loss sum(out^2); U(-1,1), N(0, 0.05^2), seed 4
+  64x64 input, global batch 1024, loss sum of squares of the output (scaled
+  by an exact power of two, see ``stack_loss``); U(-1,1), N(0, 0.05^2), seed 4
 
 Draw order on a CPU ``torch.Generator`` seeded per case: the unpadded input,
 then the flat parameter vector of each layer, then the upstream gradient
@@ -106,6 +107,22 @@ def draw_grad(wl: Workload, g: torch.Generator, n: int = None, dtype=torch.float
 
 def pad_input(x: torch.Tensor, p: int) -> torch.Tensor:
     return torch.nn.functional.pad(x, (p, p, p, p))
+
+
+# Loss of the c5 stack.  sum(out^2) itself is about 4e56 at the full batch and
+# every parameter gradient lies between 1e41 and 1e57: far beyond the fp32
+# range (3.4e38), so in fp32 the loss is inf and all parameter gradients are
+# inf/NaN, in the reference CPU op as much as here.  The stack's loss is
+# therefore sum((2^-40 out)^2) = 2^-80 sum(out^2): multiplying by a power of
+# two is exact, so every gradient is exactly 2^-80 times that of sum(out^2)
+# wherever the latter is representable, and the step does the same work.
+STACK_OUTPUT_SCALE = 2.0 ** -40
+
+
+def stack_loss(y: torch.Tensor) -> torch.Tensor:
+    """sum((2^-40 y)^2), the c5 training loss (see STACK_OUTPUT_SCALE)."""
+    ys = y * STACK_OUTPUT_SCALE
+    return (ys * ys).sum()
 
 
 def fwd_flops_per_image(wl: Workload, i: int = 0) -> float:

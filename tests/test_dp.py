@@ -92,3 +92,32 @@ def test_shard_bounds_cover_the_batch():
             assert all(a[1] == b[0] for a, b in zip(got, got[1:]))
             sizes = [b - a for a, b in got]
             assert max(sizes) - min(sizes) <= 1
+
+
+def _worker_missing(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        model = make_model()
+        red = GradAllReduce(model.parameters(), bucketed=True)
+        if rank == 0:
+            x = shard(batch(), rank, world)
+            (model(x) ** 2).sum().backward()
+        # rank 1 has no gradient at all this step: it still joins the same
+        # collective (zeros) and receives rank 0's sum
+        red()
+        out[rank] = torch.cat([p.grad.reshape(-1) for p in model.parameters()])
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bucket_spans_parameters_without_gradient():
+    model = make_model()
+    (model(shard(batch(), 0, 2)) ** 2).sum().backward()
+    ref = torch.cat([p.grad.reshape(-1) for p in model.parameters()])
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker_missing, args=(2, _free_port(), out), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        assert torch.allclose(out[r], ref, rtol=1e-12, atol=1e-12)
