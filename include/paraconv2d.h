@@ -123,6 +123,34 @@ int pc2d_backward(int dtype, const void *grad, const void *input, const void *pa
                   int n, int channels, int height, int width, int m, int skip_input_grad,
                   void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes, void *stream);
 
+/* The two steps of the reference module's forward before the op
+ * (ptparaconv2d.py:216-217: `x = input_factor * input`, then a constant-zero
+ * F.pad) as one pass: output[n][c][y][x] = scale * input[n][c][y - pad_top]
+ * [x - pad_left] inside, 0 in the padding; output is
+ * [n][channels][height+pad_top+pad_bottom][width+pad_left+pad_right].  fp32 or
+ * fp64; pads must be >= 0 (F.pad's negative pads crop; use torch for those). */
+int pc2d_pad_scale(int dtype, const void *input, int n, int channels, int height, int width,
+                   int pad_top, int pad_bottom, int pad_left, int pad_right, double scale,
+                   void *output, void *stream);
+
+/* Backward pass of the reference module around the op
+ * (ptparaconv2d.py:52-58 and the backward of its pad and input factor,
+ * :216-217): as pc2d_backward on the padded input, but the input gradient is
+ * written only for the unpadded input, rows pad_top .. height-pad_bottom-1
+ * and columns pad_left .. width-pad_right-1, into an
+ * [n][channels][height-pad_top-pad_bottom][width-pad_left-pad_right] array,
+ * multiplied by dx_scale (the module's input_factor * grad_factor).  This
+ * replaces the module's slice of the padded gradient and its two scalings
+ * (three passes over the input gradient) with the kernels' own stores.  With
+ * skip_input_grad nonzero, inputgrad is zero-filled, or left alone when it is
+ * NULL (a caller that does not need it).  Workspace: as pc2d_backward. */
+int pc2d_backward_interior(int dtype, const void *grad, const void *input, const void *pars, const void *hsum,
+                           double factor, int k0, int k1, int s0, int s1, int dl0, int dl1,
+                           int n, int channels, int height, int width, int m, int skip_input_grad,
+                           int pad_top, int pad_bottom, int pad_left, int pad_right, double dx_scale,
+                           void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes,
+                           void *stream);
+
 /* Human-readable name of a pc2d_status. */
 const char *pc2d_status_string(int status);
 

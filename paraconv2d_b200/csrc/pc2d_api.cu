@@ -246,14 +246,21 @@ size_t pc2d_backward_workspace_size(int dtype, int n, int channels, int height, 
   return simt_backward_workspace<double>(p, skip_input_grad != 0);
 }
 
-int pc2d_backward(int dtype, const void *grad, const void *input, const void *pars, const void *hsum, double factor,
+}  // extern "C"
+
+namespace {
+
+// Backward pass with the input gradient written as `dxo` describes; with
+// dx_optional, inputgrad may be null when skip_input_grad is set.
+int backward_impl(int dtype, const void *grad, const void *input, const void *pars, const void *hsum, double factor,
                   int k0, int k1, int s0, int s1, int dl0, int dl1, int n, int channels, int height, int width, int m,
-                  int skip_input_grad, void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes,
-                  void *stream) {
+                  int skip_input_grad, const DxOut *dxo_in, bool dx_optional, void *inputgrad, void *parsgrad,
+                  void *workspace, size_t workspace_bytes, void *stream) {
   Problem p;
   int st = validate(dtype, n, channels, height, width, m, k0, k1, s0, s1, dl0, dl1, &p);
   if (st != PC2D_OK) return st;
-  const bool need_dx = p.NHW > 0;
+  const DxOut dxo = dxo_in ? *dxo_in : dx_full(p);
+  const bool need_dx = (int64_t)p.n * dxo.CHWu > 0 && !(dx_optional && skip_input_grad && !inputgrad);
   const bool need_dp = m > 0;
   if ((need_dx && !inputgrad) || (need_dp && !parsgrad) || (p.NPQ > 0 && m > 0 && (!grad || !input || !pars || !hsum))) {
     set_last_error("null tensor pointer");
@@ -265,7 +272,8 @@ int pc2d_backward(int dtype, const void *grad, const void *input, const void *pa
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (m == 0) {
-    if (need_dx) PC2D_CUDA_CHECK(cudaMemsetAsync(inputgrad, 0, (dtype == PC2D_DTYPE_F32 ? 4 : 8) * (size_t)p.NHW * p.C, s));
+    if (need_dx)
+      PC2D_CUDA_CHECK(cudaMemsetAsync(inputgrad, 0, (dtype == PC2D_DTYPE_F32 ? 4 : 8) * (size_t)p.n * dxo.CHWu, s));
     return PC2D_OK;
   }
   if (use_tc_bwd(p, dtype)) {
@@ -275,7 +283,7 @@ int pc2d_backward(int dtype, const void *grad, const void *input, const void *pa
       return PC2D_ERR_WORKSPACE;
     }
     return tc_backward(p, (const float *)grad, (const float *)input, (const float *)pars, (const float *)hsum, factor,
-                       skip_input_grad != 0, (float *)inputgrad, (float *)parsgrad, workspace, workspace_bytes, s);
+                       skip_input_grad != 0, (float *)inputgrad, (float *)parsgrad, workspace, workspace_bytes, s, dxo);
   }
   if (g_algo.load() == PC2D_ALGO_TC) {
     set_last_error("tensor-core backward requested but not available for this problem");
@@ -284,10 +292,67 @@ int pc2d_backward(int dtype, const void *grad, const void *input, const void *pa
   if (dtype == PC2D_DTYPE_F32)
     return simt_backward<float>(p, (const float *)grad, (const float *)input, (const float *)pars,
                                 (const float *)hsum, factor, skip_input_grad != 0, (float *)inputgrad,
-                                (float *)parsgrad, workspace, workspace_bytes, s);
+                                (float *)parsgrad, workspace, workspace_bytes, s, dxo);
   return simt_backward<double>(p, (const double *)grad, (const double *)input, (const double *)pars,
                                (const double *)hsum, factor, skip_input_grad != 0, (double *)inputgrad,
-                               (double *)parsgrad, workspace, workspace_bytes, s);
+                               (double *)parsgrad, workspace, workspace_bytes, s, dxo);
+}
+
+}  // namespace
+
+extern "C" {
+
+int pc2d_backward(int dtype, const void *grad, const void *input, const void *pars, const void *hsum, double factor,
+                  int k0, int k1, int s0, int s1, int dl0, int dl1, int n, int channels, int height, int width, int m,
+                  int skip_input_grad, void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes,
+                  void *stream) {
+  return backward_impl(dtype, grad, input, pars, hsum, factor, k0, k1, s0, s1, dl0, dl1, n, channels, height, width,
+                       m, skip_input_grad, nullptr, false, inputgrad, parsgrad, workspace, workspace_bytes, stream);
+}
+
+int pc2d_backward_interior(int dtype, const void *grad, const void *input, const void *pars, const void *hsum,
+                           double factor, int k0, int k1, int s0, int s1, int dl0, int dl1, int n, int channels,
+                           int height, int width, int m, int skip_input_grad, int pad_top, int pad_bottom,
+                           int pad_left, int pad_right, double dx_scale, void *inputgrad, void *parsgrad,
+                           void *workspace, size_t workspace_bytes, void *stream) {
+  if (pad_top < 0 || pad_bottom < 0 || pad_left < 0 || pad_right < 0 || pad_top + pad_bottom > height ||
+      pad_left + pad_right > width) {
+    set_last_error("invalid padding %d/%d/%d/%d of a %dx%d input", pad_top, pad_bottom, pad_left, pad_right, height,
+                   width);
+    return PC2D_ERR_INVALID_ARGUMENT;
+  }
+  DxOut o;
+  o.pt = pad_top;
+  o.pl = pad_left;
+  o.Hu = height - pad_top - pad_bottom;
+  o.Wu = width - pad_left - pad_right;
+  o.HWu = (int64_t)o.Hu * o.Wu;
+  o.CHWu = (int64_t)(channels > 0 ? channels : 0) * o.HWu;
+  o.scale = dx_scale;
+  return backward_impl(dtype, grad, input, pars, hsum, factor, k0, k1, s0, s1, dl0, dl1, n, channels, height, width,
+                       m, skip_input_grad, &o, true, inputgrad, parsgrad, workspace, workspace_bytes, stream);
+}
+
+int pc2d_pad_scale(int dtype, const void *input, int n, int channels, int height, int width, int pad_top,
+                   int pad_bottom, int pad_left, int pad_right, double scale, void *output, void *stream) {
+  if (dtype != PC2D_DTYPE_F32 && dtype != PC2D_DTYPE_F64) {
+    set_last_error("unsupported dtype %d (float32 and float64 only)", dtype);
+    return PC2D_ERR_INVALID_ARGUMENT;
+  }
+  if (n < 0 || channels < 0 || height < 0 || width < 0 || pad_top < 0 || pad_bottom < 0 || pad_left < 0 ||
+      pad_right < 0) {
+    set_last_error("invalid shape or padding");
+    return PC2D_ERR_INVALID_ARGUMENT;
+  }
+  const int64_t rows = (int64_t)n * channels * (height + pad_top + pad_bottom);
+  const int Wp = width + pad_left + pad_right;
+  if (rows == 0 || Wp == 0) return PC2D_OK;
+  if (!output || (!input && (int64_t)n * channels * height * width > 0)) {
+    set_last_error("null tensor pointer");
+    return PC2D_ERR_INVALID_ARGUMENT;
+  }
+  return pad_scale(dtype, input, n, channels, height, width, pad_top, pad_bottom, pad_left, pad_right, scale, output,
+                   reinterpret_cast<cudaStream_t>(stream));
 }
 
 const char *pc2d_status_string(int status) {

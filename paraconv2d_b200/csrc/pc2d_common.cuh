@@ -97,6 +97,29 @@ inline Problem make_problem(int n, int C, int H, int W, int m, int k0, int k1, i
   return p;
 }
 
+// Where the input gradient goes.  The kernels compute it over the padded
+// input [n][C][H][W] the op receives.  For the op itself the whole of it is
+// written, as is.  A module that pads its input before the op (reference
+// ptparaconv2d.py:216-218) needs only the gradient of the unpadded input,
+// times its input factor and grad factor: rows pt .. pt+Hu-1 and columns
+// pl .. pl+Wu-1, written into an [n][C][Hu][Wu] array and multiplied by
+// `scale`, which saves the module two passes over dx (slice, scale).
+struct DxOut {
+  int pt, pl, Hu, Wu;
+  int64_t HWu, CHWu;
+  double scale;
+};
+
+inline DxOut dx_full(const Problem &p) { return DxOut{0, 0, p.H, p.W, p.HW, p.CHW, 1.0}; }
+
+// Index in the input-gradient array of padded pixel (y, x), channel 0, of
+// image n; -1 when the pixel lies in the padding.
+__host__ __device__ __forceinline__ int64_t dx_index(const DxOut &o, int64_t n, int y, int x) {
+  const int yi = y - o.pt, xi = x - o.pl;
+  if ((unsigned)yi >= (unsigned)o.Hu || (unsigned)xi >= (unsigned)o.Wu) return -1;
+  return n * o.CHWu + (int64_t)yi * o.Wu + xi;
+}
+
 // Offset, within one input channel plane, of tap `tap` (= ix2*k1 + iy2) of the
 // window of output pixel (0,0).  The window is flipped: tap (ix2, iy2) reads
 // row (k0-1-ix2)*dl0 and column (k1-1-iy2)*dl1 (reference paraconv2d.cc:89-92,
@@ -130,12 +153,16 @@ int simt_forward(const Problem &p, const T *x, const T *pars, double factor, T *
                  cudaStream_t stream);
 template <typename T>
 size_t simt_backward_workspace(const Problem &p, bool skip_input_grad);
+// Zero-padded, scaled copy of an [n][C][H][W] input (pc2d_pad.cu).
+int pad_scale(int dtype, const void *in, int n, int C, int H, int W, int pt, int pb, int pl, int pr, double scale,
+              void *out, cudaStream_t stream);
 // With leave_dx the input gradient is neither computed nor written; with
-// skip_wgrad only the input gradient is computed.
+// skip_wgrad only the input gradient is computed.  dx is written as `dxo`
+// describes (skip_input_grad: zeros, when dx is not null).
 template <typename T>
 int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, const T *hsum,
                   double factor, bool skip_input_grad, T *dx, T *dpars, void *ws, size_t ws_bytes,
-                  cudaStream_t stream, bool leave_dx = false, bool skip_wgrad = false);
+                  cudaStream_t stream, const DxOut &dxo, bool leave_dx = false, bool skip_wgrad = false);
 
 }  // namespace pc2d
 

@@ -146,7 +146,7 @@ constexpr int DM = 64, DC = 64, DK = 16;
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 simt_dgrad_kernel(const T *__restrict__ grad, const T *__restrict__ x, const T *__restrict__ pars,
-                  const T *__restrict__ hsum, Problem p, T *__restrict__ dx) {
+                  const T *__restrict__ hsum, Problem p, DxOut dxo, T *__restrict__ dx) {
   __shared__ T a1s[DK][DM], a2s[DK][DM];
   __shared__ T bhs[DK][DC], bps[DK][DC];
   __shared__ int64_t obase[DM];
@@ -251,18 +251,22 @@ simt_dgrad_kernel(const T *__restrict__ grad, const T *__restrict__ x, const T *
     }
   }
 
+  const T two_s = T(2) * (T)dxo.scale;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t g = g0 + tx + 16 * i;
     if (g >= p.NHW) continue;
     const int64_t nn = g / p.HW;
     const int64_t r = g - nn * p.HW;
+    const int y = (int)(r / p.W);
+    const int64_t ob = dx_index(dxo, nn, y, (int)(r - (int64_t)y * p.W));
+    if (ob < 0) continue;
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int c = c0 + ty + 16 * jj;
       if (c >= p.C) continue;
       const int64_t xi = nn * p.CHW + (int64_t)c * p.HW + r;
-      dx[xi] = T(2) * (acc[i][jj] - x[xi] * sgb[i]);
+      dx[ob + (int64_t)c * dxo.HWu] = two_s * (acc[i][jj] - x[xi] * sgb[i]);
     }
   }
 }
@@ -470,15 +474,15 @@ size_t simt_backward_workspace(const Problem &p, bool) {
 template <typename T>
 int simt_backward(const Problem &p, const T *grad, const T *x, const T *pars, const T *hsum,
                   double factor, bool skip_input_grad, T *dx, T *dpars, void *ws, size_t ws_bytes,
-                  cudaStream_t stream, bool leave_dx, bool skip_wgrad) {
+                  cudaStream_t stream, const DxOut &dxo, bool leave_dx, bool skip_wgrad) {
   const size_t npars = (size_t)p.m * 2 * (p.d + 1);
   if (leave_dx) {
   } else if (skip_input_grad || p.NPQ == 0) {
-    if (p.NHW > 0) PC2D_CUDA_CHECK(cudaMemsetAsync(dx, 0, sizeof(T) * (size_t)p.NHW * p.C, stream));
+    if (p.NHW > 0 && dx) PC2D_CUDA_CHECK(cudaMemsetAsync(dx, 0, sizeof(T) * (size_t)p.n * dxo.CHWu, stream));
   } else {
     const dim3 grid(ceil_div(p.NHW, DM), ceil_div(p.C, DC));
     timing_begin(K_SIMT_DGRAD, stream);
-    simt_dgrad_kernel<T><<<grid, kThreads, 0, stream>>>(grad, x, pars, hsum, p, dx);
+    simt_dgrad_kernel<T><<<grid, kThreads, 0, stream>>>(grad, x, pars, hsum, p, dxo, dx);
     timing_end(K_SIMT_DGRAD, stream);
     PC2D_LAUNCH_CHECK("simt_dgrad_kernel");
   }
@@ -513,8 +517,8 @@ template int simt_forward<double>(const Problem &, const double *, const double 
 template size_t simt_backward_workspace<float>(const Problem &, bool);
 template size_t simt_backward_workspace<double>(const Problem &, bool);
 template int simt_backward<float>(const Problem &, const float *, const float *, const float *, const float *, double, bool,
-                                  float *, float *, void *, size_t, cudaStream_t, bool, bool);
+                                  float *, float *, void *, size_t, cudaStream_t, const DxOut &, bool, bool);
 template int simt_backward<double>(const Problem &, const double *, const double *, const double *, const double *, double,
-                                   bool, double *, double *, void *, size_t, cudaStream_t, bool, bool);
+                                   bool, double *, double *, void *, size_t, cudaStream_t, const DxOut &, bool, bool);
 
 }  // namespace pc2d

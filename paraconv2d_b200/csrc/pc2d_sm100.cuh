@@ -301,5 +301,24 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 // value the tensor core sees exactly); lo = v - hi is exact in fp32.
 __device__ __forceinline__ uint32_t tf32_hi_bits(float v) { return __float_as_uint(v) & 0xFFFFE000u; }
 
+// Nearest tf32 value of v (ties away from zero), as fp32 bits with the low 13
+// bits zero: the tensor core reads exactly this value.
+__device__ __forceinline__ uint32_t tf32_rna_bits(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return r;
+}
+
+// Split of an operand prepared once per call (the weights): hi and lo are both
+// rounded to nearest, so each is within 2^-11 of its part and the product of
+// two split operands (hi*hi + lo*hi + hi*lo) is within about 2^-21 of the
+// exact product.  The producers' per-element split (tf32_hi_bits, lo = v - hi,
+// read by the tensor core with its low 13 bits ignored) trades up to 2^-20
+// for half the instructions.
+__device__ __forceinline__ void tf32_split_rn(float v, float &hi, float &lo) {
+  hi = __uint_as_float(tf32_rna_bits(v));
+  lo = __uint_as_float(tf32_rna_bits(v - hi));
+}
+
 }  // namespace sm100
 }  // namespace pc2d

@@ -18,19 +18,37 @@ bool tc_backward_supported(const Problem &p);
 size_t tc_backward_workspace(const Problem &p, bool skip_input_grad);
 int tc_backward(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum,
                 double factor, bool skip_input_grad, float *dx, float *dpars, void *ws, size_t ws_bytes,
-                cudaStream_t stream);
+                cudaStream_t stream, const DxOut &dxo);
 
 // Input gradient of narrow inputs (C <= 8): GEMM over output pixels + col2im
 // (pc2d_tc_dgcol.cu).
 bool tc_dgcol_supported(const Problem &p);
 size_t tc_dgcol_workspace(const Problem &p);
-int tc_dgcol(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, float *dx,
-             void *ws, cudaStream_t stream);
+int tc_dgcol(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum,
+             const DxOut &dxo, float *dx, void *ws, cudaStream_t stream);
 
 // Parameter-gradient GEMM and its reduction (pc2d_tc_wgrad.cu).
 bool tc_wgrad_supported(const Problem &p);
 size_t tc_wgrad_workspace(const Problem &p);
 int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, double factor,
+             float *dpars, void *ws, cudaStream_t stream);
+
+// Fixed-order fp64 reduction of per-segment parameter-gradient partials and
+// the epilogue dh = 2f dH, dp = 2f (dP - p SG), dh0 = 2f S1, dp0 = -2f p0 SG
+// (pc2d_tc_wgrad.cu).  Layout: for segment s and window range nr, channel
+// block mb (item = (s*nNR + nr)*nmb + mb), part[(item*128 + r)*NR + kl] holds
+// sum_o A[r,o] win_o[nr*NR + kl] and sums[item*128 + r] the row sum of A,
+// with rows r = [g*hsum of the block's JM channels; g of the same channels].
+// Launched as a programmatic dependent of the kernel that writes the
+// partials; it waits for that kernel before reading them.
+int tc_wgrad_reduce(const Problem &p, const float *part, const float *sums, const float *pars, double factor,
+                    float *dpars, int64_t nseg, int nNR, int nmb, int JM, int NR, cudaStream_t stream);
+
+// Parameter gradients of narrow windows (d <= 31 window elements, m <= 32
+// output channels) on the CUDA cores (pc2d_nw_wgrad.cu).
+bool nw_wgrad_supported(const Problem &p);
+size_t nw_wgrad_workspace(const Problem &p);
+int nw_wgrad(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, double factor,
              float *dpars, void *ws, cudaStream_t stream);
 
 // A kernel that waits on an mbarrier nothing completes, bounded by timeout_us.

@@ -183,10 +183,11 @@ __global__ void __launch_bounds__(256) tc_dg_prep_weights(const float *__restric
     const int j = jb * kJB + kk / 2;
     float v = 0.f;
     if (ch < p.C && j < p.m) v = ((kk & 1) ? pp : h)[(int64_t)j * p.d + (int64_t)ch * p.T + tap];
-    const float hi = __uint_as_float(tf32_hi_bits(v));
+    float hi, lo;
+    tf32_split_rn(v, hi, lo);
     const int pos = r * 32 + (((kk >> 2) ^ (r & 7)) << 2) + (kk & 3);
     blk[pos] = hi;
-    blk[c.NC * 32 + pos] = v - hi;
+    blk[c.NC * 32 + pos] = lo;
   }
 }
 
@@ -271,7 +272,7 @@ template <int NC>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, const float *__restrict__ hsum,
                 const float *__restrict__ wsB, Problem p, DgCfg c, const __grid_constant__ CUtensorMap gmap,
-                const __grid_constant__ CUtensorMap hmap, float *__restrict__ dx, int *status) {
+                const __grid_constant__ CUtensorMap hmap, DxOut dxo, float *__restrict__ dx, int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -416,6 +417,7 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     // lanes 32*(w%4) .. +31), each draining and writing half of the block's
     // channels.
     constexpr int NH = NC / 2;
+    const float two_s = 2.f * (float)dxo.scale;  // 2 (x input factor x grad factor, for a padding module)
     const int qq = warp % 4, half = warp >= 11 ? 1 : 0;
     const int c0 = half * NH;  // this warp's first channel within the block
     const int r = qq * 32 + lane;
@@ -432,10 +434,12 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       // back only what it copied, so the cp.async wait alone orders them)
       const int q = tg.q0 + r;
       const bool pv = q < tg.npix;
-      int64_t xb = 0;
+      int64_t xb = 0, ob = -1;
       if (pv) {
         const int ay = q / tg.cols;
-        xb = tg.n * p.CHW + (int64_t)(tg.py + p.s0 * ay) * p.W + tg.px + p.s1 * (q - ay * tg.cols);
+        const int yy = tg.py + p.s0 * ay, xx = tg.px + p.s1 * (q - ay * tg.cols);
+        xb = tg.n * p.CHW + (int64_t)yy * p.W + xx;
+        ob = dx_index(dxo, tg.n, yy, xx);
 #pragma unroll 8
         for (int cc = c0; cc < c0 + NH; ++cc) {
           const bool have = cb * NC + cc < p.C;
@@ -483,11 +487,11 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       const float sg = sgbuf[tb * kTileM + r];
       mbar_arrive(&sg_empty[tb]);
       cp_async_wait<0>();
-      if (pv) {
+      if (ob >= 0) {
 #pragma unroll
         for (int cc = 0; cc < NH; ++cc)
           if (cb * NC + c0 + cc < p.C)
-            dx[xb + (int64_t)(cb * NC + c0 + cc) * p.HW] = 2.f * (acc[cc] - sx[(c0 + cc) * kTileM + r] * sg);
+            dx[ob + (int64_t)(cb * NC + c0 + cc) * dxo.HWu] = two_s * (acc[cc] - sx[(c0 + cc) * kTileM + r] * sg);
       }
     }
     cp_async_wait<0>();  // copies of an item left on an error path
@@ -673,7 +677,7 @@ PerContext<uint64_t> g_attr;
 
 template <int NC>
 int launch_dgrad(const Problem &p, DgCfg c, const float *grad, const float *x, const float *hsum,
-                 const float *wsB, float *dx, int *status, cudaStream_t stream) {
+                 const float *wsB, const DxOut &dxo, float *dx, int *status, cudaStream_t stream) {
   const int ast = once_per_context(g_attr, 1ull << (NC / 16 - 1), []() -> int {
     PC2D_CUDA_CHECK(cudaFuncSetAttribute(tc_dgrad_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     return (int)PC2D_OK;
@@ -687,7 +691,7 @@ int launch_dgrad(const Problem &p, DgCfg c, const float *grad, const float *x, c
     c.tma = 0;  // per-plane bulk copies instead (same slot size)
   const int grid = (int)std::min<int64_t>(c.items, device_sm_count());
   timing_begin(K_DGRAD, stream);
-  tc_dgrad_kernel<NC><<<grid, kThreads, dg_smem_bytes(c), stream>>>(grad, x, hsum, wsB, p, c, gmap, hmap, dx,
+  tc_dgrad_kernel<NC><<<grid, kThreads, dg_smem_bytes(c), stream>>>(grad, x, hsum, wsB, p, c, gmap, hmap, dxo, dx,
                                                                       status);
   timing_end(K_DGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_dgrad_kernel");
@@ -703,11 +707,14 @@ bool dg_supported(const Problem &p) {
 
 }  // namespace
 
-bool tc_backward_supported(const Problem &p) { return dg_supported(p) || tc_wgrad_supported(p); }
+bool tc_backward_supported(const Problem &p) {
+  return dg_supported(p) || tc_wgrad_supported(p) || nw_wgrad_supported(p);
+}
 
 namespace {
 // Workspace layout: [parameter-gradient scratch | dgrad weights]
 size_t wgrad_scratch(const Problem &p, bool skip_input_grad) {
+  if (nw_wgrad_supported(p)) return align_up(nw_wgrad_workspace(p), 256);
   return align_up(tc_wgrad_supported(p) ? tc_wgrad_workspace(p) : simt_backward_workspace<float>(p, skip_input_grad),
                   256);
 }
@@ -724,15 +731,15 @@ size_t tc_backward_workspace(const Problem &p, bool skip_input_grad) {
 
 int tc_backward(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum,
                 double factor, bool skip_input_grad, float *dx, float *dpars, void *ws, size_t ws_bytes,
-                cudaStream_t stream) {
+                cudaStream_t stream, const DxOut &dxo) {
   const size_t wscr = wgrad_scratch(p, skip_input_grad);
   bool dx_done = false;
   if (skip_input_grad || p.NPQ == 0) {
-    if (p.NHW > 0) PC2D_CUDA_CHECK(cudaMemsetAsync(dx, 0, sizeof(float) * (size_t)p.NHW * p.C, stream));
+    if (p.NHW > 0 && dx) PC2D_CUDA_CHECK(cudaMemsetAsync(dx, 0, sizeof(float) * (size_t)p.n * dxo.CHWu, stream));
     dx_done = true;
   } else if (tc_dgcol_supported(p)) {
     // few input channels: dense GEMM over the output pixels + col2im
-    const int st = tc_dgcol(p, grad, x, pars, hsum, dx, reinterpret_cast<char *>(ws) + wscr, stream);
+    const int st = tc_dgcol(p, grad, x, pars, hsum, dxo, dx, reinterpret_cast<char *>(ws) + wscr, stream);
     if (st != PC2D_OK) return st;
     dx_done = true;
   } else if (dg_supported(p)) {
@@ -747,25 +754,29 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
     PC2D_LAUNCH_CHECK("tc_dg_prep_weights");
     int st = PC2D_OK;
     switch (c.NC) {
-      case 16: st = launch_dgrad<16>(p, c, grad, x, hsum, wsB, dx, status, stream); break;
-      case 32: st = launch_dgrad<32>(p, c, grad, x, hsum, wsB, dx, status, stream); break;
-      case 48: st = launch_dgrad<48>(p, c, grad, x, hsum, wsB, dx, status, stream); break;
-      case 64: st = launch_dgrad<64>(p, c, grad, x, hsum, wsB, dx, status, stream); break;
+      case 16: st = launch_dgrad<16>(p, c, grad, x, hsum, wsB, dxo, dx, status, stream); break;
+      case 32: st = launch_dgrad<32>(p, c, grad, x, hsum, wsB, dxo, dx, status, stream); break;
+      case 48: st = launch_dgrad<48>(p, c, grad, x, hsum, wsB, dxo, dx, status, stream); break;
+      case 64: st = launch_dgrad<64>(p, c, grad, x, hsum, wsB, dxo, dx, status, stream); break;
       default: set_last_error("internal: unsupported channel block %d", c.NC); return PC2D_ERR_UNSUPPORTED;
     }
     if (st != PC2D_OK) return st;
     dx_done = true;
   }
-  if (p.NPQ > 0 && tc_wgrad_supported(p)) {
+  // parameter gradients: narrow windows on the CUDA cores, else the
+  // tensor-core GEMM
+  const bool nw = nw_wgrad_supported(p);
+  if (p.NPQ > 0 && (nw || tc_wgrad_supported(p))) {
     if (!dx_done) {
-      // input gradient on the CUDA cores, then the tensor-core parameter gradients
-      const int st = simt_backward<float>(p, grad, x, pars, hsum, factor, false, dx, dpars, nullptr, 0, stream,
+      // input gradient on the CUDA cores, then the parameter gradients
+      const int st = simt_backward<float>(p, grad, x, pars, hsum, factor, false, dx, dpars, nullptr, 0, stream, dxo,
                                           /*leave_dx=*/false, /*skip_wgrad=*/true);
       if (st != PC2D_OK) return st;
     }
+    if (nw) return nw_wgrad(p, grad, x, pars, hsum, factor, dpars, ws, stream);
     return tc_wgrad(p, grad, x, pars, hsum, factor, dpars, ws, stream);
   }
-  return simt_backward<float>(p, grad, x, pars, hsum, factor, skip_input_grad, dx, dpars, ws, wscr, stream,
+  return simt_backward<float>(p, grad, x, pars, hsum, factor, skip_input_grad, dx, dpars, ws, wscr, stream, dxo,
                               /*leave_dx=*/dx_done);
 }
 

@@ -106,10 +106,11 @@ __global__ void __launch_bounds__(256) tc_dc_prep_weights(const float *__restric
       if (n < c.NY - 1) v = (w == 0 ? h : pp)[(int64_t)j * p.d + n];
       else if (n == c.NY - 1) v = w == 1 ? 1.f : 0.f;
     }
-    const float hi = __uint_as_float(tf32_hi_bits(v));
+    float hi, lo;
+    tf32_split_rn(v, hi, lo);
     const int pos = n * 32 + (((kk >> 2) ^ (n & 7)) << 2) + (kk & 3);
     blk[pos] = hi;
-    blk[c.NP * 32 + pos] = v - hi;
+    blk[c.NP * 32 + pos] = lo;
   }
 }
 
@@ -447,7 +448,7 @@ __device__ __forceinline__ void col2im_taps(const float *__restrict__ yb, const 
 
 template <int CC>
 __global__ void __launch_bounds__(kColThreads) tc_dc_col2im(const float *__restrict__ Y, const float *__restrict__ x,
-                                                            Problem p, DcCfg c, float *__restrict__ dx) {
+                                                            Problem p, DcCfg c, DxOut dout, float *__restrict__ dx) {
   __shared__ int2 s_tp[kMaxT];  // (tap*PQ - (dy*Q + dx), dy*Q + dx) of the phase's taps, tap order
   __shared__ int2 s_d[kMaxT];   // (dy, dx)
   __shared__ int s_wcnt[kColThreads / 32];
@@ -510,10 +511,13 @@ __global__ void __launch_bounds__(kColThreads) tc_dc_col2im(const float *__restr
   else
     col2im_taps<CC, true>(yb, ysg, ntaps, s_tp, s_d, p.T * PQ, a, b, p.P, Q, acc, sg);
   const int y = py + p.s0 * a, xc = px + p.s1 * b;
+  const int64_t ob = dx_index(dout, n, y, xc);
+  if (ob < 0) return;  // a pixel of the padding
+  const float two_s = 2.f * (float)dout.scale;
 #pragma unroll
   for (int ci = 0; ci < CC; ++ci) {
     const int64_t xi = n * p.CHW + (int64_t)ci * p.HW + (int64_t)y * p.W + xc;
-    dx[xi] = 2.f * (acc[ci] - __ldg(x + xi) * sg);
+    dx[ob + (int64_t)ci * dout.HWu] = two_s * (acc[ci] - __ldg(x + xi) * sg);
   }
 }
 
@@ -559,8 +563,8 @@ size_t tc_dgcol_workspace(const Problem &p) {
   return align_up(dc_bsplit_bytes(c), 256) + align_up(dc_y_bytes(p, c), 256);
 }
 
-int tc_dgcol(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum, float *dx,
-             void *ws, cudaStream_t stream) {
+int tc_dgcol(const Problem &p, const float *grad, const float *x, const float *pars, const float *hsum,
+             const DxOut &dxo, float *dx, void *ws, cudaStream_t stream) {
   const DcCfg c = dc_cfg(p);
   int *status = device_status_ptr();
   if (!status) {
@@ -590,7 +594,7 @@ int tc_dgcol(const Problem &p, const float *grad, const float *x, const float *p
     const dim3 cgrid((unsigned)((ppg + kColThreads - 1) / kColThreads), (unsigned)(p.n * p.s0 * p.s1));
     switch (p.C) {
 #define PC2D_COL_CASE(k) \
-  case k: tc_dc_col2im<k><<<cgrid, kColThreads, 0, stream>>>(Y, x, p, c, dx); break;
+  case k: tc_dc_col2im<k><<<cgrid, kColThreads, 0, stream>>>(Y, x, p, c, dxo, dx); break;
       PC2D_COL_CASE(1) PC2D_COL_CASE(2) PC2D_COL_CASE(3) PC2D_COL_CASE(4)
       PC2D_COL_CASE(5) PC2D_COL_CASE(6) PC2D_COL_CASE(7) PC2D_COL_CASE(8)
 #undef PC2D_COL_CASE

@@ -163,10 +163,11 @@ __global__ void __launch_bounds__(256) tc_fwd_prep(const float *__restrict__ par
       const int64_t k = (int64_t)kc * 32 + kk;
       float v = 0.f;
       if (j < p.m && k < p.d) v = (half == 0 ? h : pp)[(int64_t)j * p.d + k];
-      const float hi = __uint_as_float(tf32_hi_bits(v));
+      float hi, lo;
+      tf32_split_rn(v, hi, lo);
       const int pos = r * 32 + (((kk >> 2) ^ (r & 7)) << 2) + (kk & 3);
       blk[pos] = hi;
-      blk[c.N * 32 + pos] = v - hi;
+      blk[c.N * 32 + pos] = lo;
     }
     return;
   }

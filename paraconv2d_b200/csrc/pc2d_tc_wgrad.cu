@@ -865,23 +865,33 @@ int tc_wgrad(const Problem &p, const float *grad, const float *x, const float *p
   }
   timing_end(K_WGRAD, stream);
   PC2D_LAUNCH_CHECK("tc_wgrad_kernel");
+  return tc_wgrad_reduce(p, part, sums, pars, factor, dpars, c.nseg, c.nNR, c.nmb, c.JM, c.NR, stream);
+}
+
+int tc_wgrad_reduce(const Problem &p, const float *part, const float *sums, const float *pars, double factor,
+                    float *dpars, int64_t nseg, int nNR, int nmb, int JM, int NR, cudaStream_t stream) {
+  WgCfg c;
+  std::memset(&c, 0, sizeof(c));
+  c.nseg = nseg;
+  c.nNR = nNR;
+  c.nmb = nmb;
+  c.JM = JM;
+  c.NR = NR;
   const dim3 fgrid(ceil_div(p.d, kFinK), p.m);
   int fq = kFinQ;
   while (fq > 2 && (int64_t)fgrid.x * fgrid.y * kFinK * fq > (int64_t)device_sm_count() * 1792) fq /= 2;
-  {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = fgrid;
-    cfg.blockDim = dim3(kFinK * fq);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tc_wgrad_finalize, part, sums, pars, p, c, fq,
-                                       2.0 * (double)(float)factor, dpars));
-  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = fgrid;
+  cfg.blockDim = dim3(kFinK * fq);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tc_wgrad_finalize, part, sums, pars, p, c, fq, 2.0 * (double)(float)factor,
+                                     dpars));
   PC2D_LAUNCH_CHECK("tc_wgrad_finalize");
   return PC2D_OK;
 }

@@ -14,6 +14,16 @@ One deliberate difference: the reference constructor runs a CPU warm-up
 forward (``ptparaconv2d.py:212-213``).  This op has no CPU kernel, so the
 warm-up runs on the current CUDA device when one is available and is skipped
 otherwise; it has no side effects either way.
+
+``ParaConv2d.forward`` computes what the reference's does: ``input_factor *
+input``, a constant ``F.pad``, the op.  With constant padding on fp32/fp64
+CUDA inputs it takes a fused route (``_PaddedParaConv2d``): the scale and the
+pad are one pass (``paraconv2d_b200.pad_scale``), and the backward writes the
+gradient of the unpadded input, times ``input_factor * grad_factor``,
+directly from the kernels (``paraconv2d_b200.backward_interior``), instead of
+slicing the padded gradient and scaling it twice.  When the input needs no
+gradient (a network's first layer), the input-gradient kernels do not run at
+all.  Other padding modes and fp16 inputs take the reference's route.
 """
 from __future__ import annotations
 
@@ -85,6 +95,35 @@ class ParaConv2dFunction(Function):
         if ctx.grad_factor != 1:
             grad_input = ctx.grad_factor * grad_input
         return grad_input, grad_pars, None, None, None, None, None, None
+
+
+class _PaddedParaConv2d(Function):
+    """input_factor * input -> constant pad -> op, with the backward of all
+    three in the op's own kernels (see the module docstring)."""
+
+    @staticmethod
+    def forward(ctx, input, pars, output_factor, kernel_size, stride, dilation, skip_input_grad, grad_factor,
+                padding, input_factor):
+        xp = torch.ops.paraconv2d_b200.pad_scale(input, list(padding), float(input_factor))
+        output, hsum = torch.ops.ptparaconv2d.forward(xp, pars, float(output_factor), kernel_size, stride, dilation)
+        ctx.save_for_backward(xp, pars, hsum)
+        ctx.output_factor = output_factor
+        ctx.kernel_size = kernel_size
+        ctx.stride = stride
+        ctx.dilation = dilation
+        ctx.skip_input_grad = skip_input_grad
+        ctx.padding = list(padding)
+        ctx.dx_scale = float(input_factor) * float(grad_factor)
+        return output
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        xp, pars, hsum = ctx.saved_tensors
+        need = bool(ctx.needs_input_grad[0])
+        grad_input, grad_pars = torch.ops.paraconv2d_b200.backward_interior(
+            grad_output, xp, pars, hsum, float(ctx.output_factor), ctx.kernel_size, ctx.stride, ctx.dilation,
+            ctx.skip_input_grad, ctx.padding, ctx.dx_scale, need)
+        return (grad_input if need else None), grad_pars, None, None, None, None, None, None, None, None
 
 
 class ParaConv2d(nn.Module):
@@ -177,7 +216,16 @@ class ParaConv2d(nn.Module):
             torch.ops.ptparaconv2d.forward(x, pars.to(dt), float(self.output_factor), self.kernel_size, self.stride,
                                            self.dilation)
 
+    def _fused(self, input):
+        return (self.padding_mode == 'constant' and input.is_cuda and input.dim() == 4
+                and input.dtype in (torch.float32, torch.float64) and self.pars.dtype == input.dtype
+                and len(self.padding) in (2, 4) and all(int(v) >= 0 for v in self.padding))
+
     def forward(self, input):
+        if self._fused(input):
+            return _PaddedParaConv2d.apply(input, self.pars, self.output_factor, self.kernel_size, self.stride,
+                                           self.dilation, self.skip_input_grad, self.grad_factor,
+                                           tuple(int(v) for v in self.padding), self.input_factor)
         x = self.input_factor * input
         x = F.pad(x, self.padding, mode=self.padding_mode)
         return ParaConv2dFunction.apply(x, self.pars, self.output_factor, self.kernel_size, self.stride,

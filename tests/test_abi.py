@@ -84,3 +84,13 @@ def test_op_has_no_cpu_fallback():
     one = torch.tensor([1, 1], dtype=torch.int)
     with pytest.raises(NotImplementedError):
         torch.ops.ptparaconv2d.forward(x, pars, 1.0, it, one, one)
+
+
+def test_module_ops_registered_beside_the_reference_schema():
+    """The module mirror's two fused steps live in their own namespace; the
+    reference's namespace keeps exactly its two ops."""
+    _lib.load_op_library()
+    assert str(torch.ops.paraconv2d_b200.pad_scale.default._schema).startswith(
+        "paraconv2d_b200::pad_scale(Tensor input, int[] padding, float scale) -> Tensor")
+    assert "need_input_grad" in str(torch.ops.paraconv2d_b200.backward_interior.default._schema)
+    assert str(torch.ops.ptparaconv2d.forward.default._schema) == REF_FORWARD_SCHEMA

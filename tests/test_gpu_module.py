@@ -107,3 +107,122 @@ def test_op_rejects_bad_arguments():
         torch.ops.ptparaconv2d.forward(x, torch.zeros(2 * (12 + 1)).cuda(), 1.0, k2, one, one)
     with pytest.raises(NotImplementedError):
         torch.ops.ptparaconv2d.forward(x.bfloat16(), torch.zeros(2 * 28).cuda().bfloat16(), 1.0, k3, one, one)
+
+
+def _reference_route(m, x):
+    """The reference module's route: input_factor * x, F.pad, the op's
+    autograd Function (ptparaconv2d.py:215-218)."""
+    xx = F.pad(m.input_factor * x, m.padding, mode=m.padding_mode)
+    return pc.ParaConv2dFunction.apply(xx, m.pars, m.output_factor, m.kernel_size, m.stride, m.dilation,
+                                       m.skip_input_grad, m.grad_factor)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+@pytest.mark.parametrize("cin", [5, 16], ids=["narrow_input", "implicit_dgrad"])
+@pytest.mark.parametrize("kw", [
+    dict(padding=1),
+    dict(padding=(1, 2)),
+    dict(padding=(2, 0, 1, 3), stride=2),
+    dict(padding=1, input_factor=1.7, grad_factor=0.5, output_factor=0.3),
+])
+def test_fused_route_equals_reference_route(kw, cin, dtype):
+    """The module's fused route (one pad+scale pass; input gradient written
+    unpadded and scaled by the kernels) gives the reference route's results:
+    outputs and parameter gradients bitwise, the input gradient to within two
+    roundings (the scale is applied once, as 2*input_factor*grad_factor)."""
+    m = _module(cin, 24, 3, **kw).to(dtype)
+    assert m._fused(torch.zeros(1, cin, 4, 4, device="cuda", dtype=dtype))
+    torch.manual_seed(5)
+    x = (torch.rand(3, cin, 13, 11, dtype=dtype) * 2 - 1).cuda()
+    xa = x.clone().requires_grad_(True)
+    xb = x.clone().requires_grad_(True)
+    ya = m(xa)
+    g = torch.randn(ya.shape, dtype=dtype, device="cuda")
+    ya.backward(g)
+    ga = m.pars.grad.clone()
+    m.pars.grad = None
+    yb = _reference_route(m, xb)
+    yb.backward(g)
+    assert torch.equal(ya, yb)
+    assert torch.equal(ga, m.pars.grad)
+    eps = torch.finfo(dtype).eps
+    assert float((xa.grad - xb.grad).abs().max()) <= 4 * eps * float(xb.grad.abs().max())
+
+
+def test_fused_route_first_layer_skips_input_gradient():
+    """An input that needs no gradient: the input-gradient kernels do not run,
+    and the parameter gradient is the same (bitwise) as when they do."""
+    m = _module(3, 8, 3, padding=1)
+    x = (torch.rand(2, 3, 16, 16) * 2 - 1).cuda()
+    y = m(x)
+    g = torch.randn(y.shape, device="cuda")
+    y.backward(g)
+    ga = m.pars.grad.clone()
+    m.pars.grad = None
+    xr = x.clone().requires_grad_(True)
+    m(xr).backward(g)
+    assert torch.equal(ga, m.pars.grad)
+    assert xr.grad is not None and float(xr.grad.abs().max()) > 0
+
+
+def test_fused_route_skip_input_grad_gives_zeros():
+    m = _module(3, 4, 3, padding=1, skip_input_grad=True)
+    x = torch.rand(2, 3, 8, 8, device="cuda", requires_grad=True)
+    m(x).sum().backward()
+    assert x.grad is not None and x.grad.shape == x.shape and torch.count_nonzero(x.grad) == 0
+
+
+def test_other_padding_modes_take_the_reference_route():
+    m = _module(3, 4, 3, padding=1, padding_mode='reflect')
+    x = torch.rand(2, 3, 8, 8, device="cuda")
+    assert not m._fused(x)
+    y = m(x)
+    out, _ = _oracle_layer(m, x.cpu())
+    assert elementwise_excess(y.detach().cpu().numpy(), out) <= 1.0
+
+
+@pytest.mark.parametrize("dtype,code", [(torch.float32, 0), (torch.float64, 1)])
+def test_cabi_pad_scale_and_interior_backward(dtype, code):
+    """pc2d_pad_scale equals F.pad(scale * x) bitwise; pc2d_backward_interior
+    equals pc2d_backward's padded input gradient, sliced and scaled (bitwise
+    for scale 1), with the same parameter gradient."""
+    from cabi_runner import backward, forward
+    from paraconv2d_b200 import _lib
+
+    lib = _lib.cabi()
+    torch.manual_seed(9)
+    n, C, H, W, m_, k = 2, 6, 10, 9, 7, 3
+    pt, pb, pl, pr = 1, 2, 0, 3
+    x = (torch.rand(n, C, H, W, dtype=dtype) * 2 - 1).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    for scale in (1.0, 0.375):
+        xp = torch.empty(n, C, H + pt + pb, W + pl + pr, dtype=dtype, device="cuda")
+        assert lib.pc2d_pad_scale(code, x.data_ptr(), n, C, H, W, pt, pb, pl, pr, scale, xp.data_ptr(), stream) == 0
+        assert torch.equal(xp, F.pad(scale * x, (pl, pr, pt, pb)))
+    pars = (torch.randn(2 * m_ * (C * k * k + 1), dtype=dtype) * 0.1).cuda()
+    out, hsum = forward(xp, pars, 1.0, k)
+    g = torch.randn(out.shape, dtype=dtype, device="cuda")
+    dx_full, dp_full = backward(g, xp, pars, hsum, 1.0, k)
+    Hp, Wp = xp.shape[2], xp.shape[3]
+    wsb = lib.pc2d_backward_workspace_size(code, n, C, Hp, Wp, m_, k, k, 1, 1, 1, 1, 0)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device="cuda")
+    for scale in (1.0, 2.5):
+        dx = torch.full((n, C, H, W), float("nan"), dtype=dtype, device="cuda")
+        dp = torch.empty_like(pars)
+        st = lib.pc2d_backward_interior(code, g.data_ptr(), xp.data_ptr(), pars.data_ptr(), hsum.data_ptr(), 1.0,
+                                        k, k, 1, 1, 1, 1, n, C, Hp, Wp, m_, 0, pt, pb, pl, pr, scale, dx.data_ptr(),
+                                        dp.data_ptr(), ws.data_ptr(), wsb, stream)
+        assert st == 0, _lib.status_message(st)
+        ref = dx_full[:, :, pt:Hp - pb, pl:Wp - pr] * scale
+        if scale == 1.0:
+            assert torch.equal(dx, ref)
+        else:
+            assert float((dx - ref).abs().max()) <= 2 * torch.finfo(dtype).eps * float(ref.abs().max())
+        assert torch.equal(dp, dp_full)
+    # skip_input_grad with no input-gradient array: parameter gradient only
+    dp = torch.empty_like(pars)
+    st = lib.pc2d_backward_interior(code, g.data_ptr(), xp.data_ptr(), pars.data_ptr(), hsum.data_ptr(), 1.0, k, k,
+                                    1, 1, 1, 1, n, C, Hp, Wp, m_, 1, pt, pb, pl, pr, 1.0, None, dp.data_ptr(),
+                                    ws.data_ptr(), wsb, stream)
+    assert st == 0, _lib.status_message(st)
+    assert torch.equal(dp, dp_full)

@@ -127,6 +127,11 @@ MEDIUM = {
     "c48_m80_k3_s2": dict(n=2, C=48, H=21, W=21, m=80, k=(3, 3), s=(2, 2), dl=(1, 1)),
     # few input channels: the output-pixel GEMM + col2im input gradient
     "c5_m24_k5x3_s1x2_dl2x1_narrow": dict(n=16, C=5, H=60, W=60, m=24, k=(5, 3), s=(1, 2), dl=(2, 1)),
+    # narrow windows (d <= 31, m <= 32): CUDA-core parameter gradients; 154
+    # output pixels per image (not a multiple of 4: element-wise staging)
+    "c1_m20_k5_s2_dl2x1_window25": dict(n=3, C=1, H=29, W=31, m=20, k=(5, 5), s=(2, 2), dl=(2, 1)),
+    # the widest such window (31 elements, ones column at 31), 32 channels
+    "c31_m32_k1_window31": dict(n=2, C=31, H=12, W=12, m=32, k=(1, 1), s=(1, 1), dl=(1, 1)),
 }
 
 
