@@ -100,6 +100,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="c2")
+    ap.add_argument("--layer", type=int, default=None,
+                    help="benchmark this layer of a multi-layer workload on its own (single-layer line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-stack", action="store_true", help="skip the data-parallel stack block")
     ap.add_argument("--stack-steps", type=int, default=20)
@@ -690,6 +692,8 @@ def run_ours(args):
     workloads = load_workloads()
     lib = _lib.cabi()
     wl = workloads.WORKLOADS[args.workload]
+    if args.layer is not None:
+        wl = workloads.layer_workload(wl, args.layer)
     if len(wl.layers) > 1:
         clk = ClockSampler(local).start()
         res = bench_stack(args, wl, lib, D, rank, world, args.steps)

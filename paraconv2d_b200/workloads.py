@@ -76,6 +76,17 @@ WORKLOADS = {
 }
 
 
+def layer_workload(wl: Workload, i: int) -> Workload:
+    """Layer i of a stack as a single-layer workload of its own: the stack's
+    batch and the layer's input size, with seeded U(-1,1) inputs (a benchmark
+    stand-in for the previous layer's output) and the stack's parameter
+    distribution."""
+    L = wl.layers[i]
+    h, w = wl.out_hw(i - 1) if i > 0 else (wl.h, wl.w)
+    return Workload(f"{wl.name}.L{i}", wl.n, h, w, (L,), wl.sigma, "uniform", wl.seed + 100 * (i + 1),
+                    f"layer {i} of {wl.name}: N={wl.n}, {L.cin}->{L.cout}ch, {h}x{w}, k{L.k} s{L.s} p{L.p}")
+
+
 def draw(wl: Workload, n: int = None, dtype=torch.float32):
     """Seeded draw of (input [n,C,H,W] unpadded, [pars per layer], generator).
     With ``n`` smaller than the workload's batch, the first n images of the

@@ -132,6 +132,8 @@ MEDIUM = {
     "c1_m20_k5_s2_dl2x1_window25": dict(n=3, C=1, H=29, W=31, m=20, k=(5, 5), s=(2, 2), dl=(2, 1)),
     # the widest such window (31 elements, ones column at 31), 32 channels
     "c31_m32_k1_window31": dict(n=2, C=31, H=12, W=12, m=32, k=(1, 1), s=(1, 1), dl=(1, 1)),
+    # strided and dilated, 40 input channels, odd m, 24 images
+    "c40_m21_k3_s2_dl1x2": dict(n=24, C=40, H=63, W=63, m=21, k=(3, 3), s=(2, 2), dl=(1, 2)),
 }
 
 
@@ -256,3 +258,4 @@ def test_backward_outputs_ordered_on_stream(name, n):
         assert torch.equal(early, late)
         sums.append(late)
     assert all(torch.equal(sums[0], s) for s in sums[1:])
+
