@@ -32,9 +32,14 @@
  *   - the return value is a pc2d_status; on failure pc2d_last_error()
  *     gives a message (thread local).  Odd kernel sizes only: even sizes make
  *     the reference read outside the window and are rejected.
- *   - kernels that wait on on-chip barriers give up after a bounded number of
- *     polls; they then record PC2D_ERR_TIMEOUT in a device-side flag that
- *     pc2d_device_status() reads (it synchronises the device).
+ *   - kernels that wait on on-chip barriers give up after a bounded time;
+ *     they then record PC2D_ERR_TIMEOUT in a device-side status word that
+ *     pc2d_device_status() reads (it synchronises the device), and in a
+ *     mirror of it in pinned host memory.  Every later compute call in that
+ *     CUDA context reads the mirror on entry (no synchronisation) and returns
+ *     PC2D_ERR_TIMEOUT until pc2d_clear_device_status() is called.  The
+ *     first compute call in a context allocates the mirror (cudaHostAlloc),
+ *     so make it before any stream capture; pc2d_forward_noalloc never does.
  */
 #ifndef PARACONV2D_B200_H_
 #define PARACONV2D_B200_H_

@@ -5,6 +5,7 @@
 #include <stdio.h>
 
 #include <atomic>
+#include <cstddef>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -16,7 +17,8 @@
 
 namespace pc2d {
 
-__device__ int g_device_status = 0;
+__device__ DeviceStatus g_device_status = {0, 0, nullptr};
+thread_local bool t_no_alloc = false;
 
 namespace {
 thread_local char t_last_error[512] = "";
@@ -48,6 +50,7 @@ cudaEvent_t timing_event() {
 }
 std::atomic<int> g_algo{PC2D_ALGO_AUTO};
 PerContext<int *> g_status_ptrs;
+PerContext<volatile int *> g_status_mirrors;  // host address of each context's mapped word
 
 // cuCtxGetCurrent and cuCtxGetId, resolved once through the runtime (the
 // library links the CUDA runtime only).
@@ -115,8 +118,32 @@ int *device_status_ptr() {
   if (cudaGetSymbolAddress(&ptr, g_device_status) != cudaSuccess) return nullptr;
   // the lookup may have made the device's primary context current
   if (!ctx) ctx = current_context_id();
-  if (ctx) g_status_ptrs.set(ctx, reinterpret_cast<int *>(ptr));
+  // the host mirror of the status word: pinned, mapped into the device, made
+  // once per context (not on the no-allocation path, which then runs without
+  // it until a regular call has made it)
+  if (ctx && !t_no_alloc) {
+    void *host = nullptr, *dev = nullptr;
+    if (cudaHostAlloc(&host, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) return nullptr;
+    *reinterpret_cast<volatile int *>(host) = 0;
+    if (cudaHostGetDevicePointer(&dev, host, 0) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_device_status, &dev, sizeof(dev), offsetof(DeviceStatus, mirror)) != cudaSuccess) {
+      cudaFreeHost(host);
+      return nullptr;
+    }
+    g_status_mirrors.set(ctx, reinterpret_cast<volatile int *>(host));
+    g_status_ptrs.set(ctx, reinterpret_cast<int *>(ptr));
+  }
   return reinterpret_cast<int *>(ptr);
+}
+
+int pending_device_error() {
+  const unsigned long long ctx = current_context_id();
+  volatile int *mirror = nullptr;
+  if (!ctx || !g_status_mirrors.get(ctx, &mirror) || *mirror == 0) return PC2D_OK;
+  set_last_error("a kernel of an earlier call gave up waiting on the device (%s); its results are invalid. "
+                 "pc2d_clear_device_status() clears this state",
+                 pc2d_status_string(*mirror));
+  return PC2D_ERR_TIMEOUT;
 }
 
 namespace {
@@ -211,6 +238,7 @@ int pc2d_forward(int dtype, const void *input, const void *pars, double factor, 
   Problem p;
   int st = validate(dtype, n, channels, height, width, m, k0, k1, s0, s1, dl0, dl1, &p);
   if (st != PC2D_OK) return st;
+  if ((st = pending_device_error()) != PC2D_OK) return st;
   if (p.NPQ == 0 || m == 0) return PC2D_OK;
   if (!input || !pars || !output || !hsum) {
     set_last_error("null tensor pointer");
@@ -259,6 +287,7 @@ int backward_impl(int dtype, const void *grad, const void *input, const void *pa
   Problem p;
   int st = validate(dtype, n, channels, height, width, m, k0, k1, s0, s1, dl0, dl1, &p);
   if (st != PC2D_OK) return st;
+  if ((st = pending_device_error()) != PC2D_OK) return st;
   const DxOut dxo = dxo_in ? *dxo_in : dx_full(p);
   const bool need_dx = (int64_t)p.n * dxo.CHWu > 0 && !(dx_optional && skip_input_grad && !inputgrad);
   const bool need_dp = m > 0;
@@ -413,7 +442,7 @@ int pc2d_timing_read(const char *kernel, double *total_ms, int *launches) {
 int pc2d_device_status(void) {
   PC2D_CUDA_CHECK(cudaDeviceSynchronize());
   int v = 0;
-  PC2D_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)));
+  PC2D_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int), offsetof(DeviceStatus, code)));
   if (v != 0) set_last_error("a device-side wait gave up (%s)", pc2d_status_string(v));
   return v;
 }
@@ -421,7 +450,10 @@ int pc2d_device_status(void) {
 int pc2d_clear_device_status(void) {
   const int zero = 0;
   PC2D_CUDA_CHECK(cudaDeviceSynchronize());
-  PC2D_CUDA_CHECK(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)));
+  PC2D_CUDA_CHECK(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int), offsetof(DeviceStatus, code)));
+  const unsigned long long ctx = current_context_id();
+  volatile int *mirror = nullptr;
+  if (ctx && g_status_mirrors.get(ctx, &mirror)) *mirror = 0;
   return PC2D_OK;
 }
 

@@ -130,13 +130,33 @@ __host__ __device__ inline int tap_col(const Problem &p, int tap) { return (p.k1
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Device-side status word of the current context: the first nonzero
-// pc2d_status a kernel records (a bounded mbarrier wait that gave up).  It is
-// a __device__ variable of the ABI translation unit; kernels get its address
-// as an argument.  Read by pc2d_device_status().
+// Device-side status of the current context: the first nonzero pc2d_status
+// a kernel records (a bounded mbarrier wait that gave up), and a mirror of it
+// in pinned host memory mapped into the device, which the entry points read
+// without synchronising.  It is a __device__ variable of the ABI translation
+// unit; kernels get its address as an int* (the code is its first word) and
+// record errors with record_device_error.  Read by pc2d_device_status().
+struct DeviceStatus {
+  int code;
+  int pad;
+  int *mirror;  // device address of the mapped host word, or null
+};
 int *device_status_ptr();
 
-__device__ __forceinline__ void record_device_error(int *status, int code) { atomicCAS(status, 0, code); }
+__device__ __forceinline__ void record_device_error(int *status, int code) {
+  atomicCAS(status, 0, code);
+  int *mirror = reinterpret_cast<DeviceStatus *>(status)->mirror;
+  if (mirror) *reinterpret_cast<volatile int *>(mirror) = code;  // a plain store: host memory
+}
+
+// PC2D_ERR_TIMEOUT (with a message) when a kernel of this context has
+// recorded a device-side error that pc2d_clear_device_status() has not
+// cleared yet, else PC2D_OK.  Reads the host mirror: no synchronisation.
+int pending_device_error();
+
+// Set by pc2d_forward_noalloc for the duration of its call: nothing on that
+// path may allocate, so the host mirror is not created there.
+extern thread_local bool t_no_alloc;
 
 // Host-side error message of the last failing ABI call on this thread.
 void set_last_error(const char *fmt, ...);

@@ -78,6 +78,11 @@ extern "C" int pc2d_forward_noalloc(int dtype, const void *input, const void *pa
   }
   void *ws = noalloc_scratch_ptr();
   if (ws == nullptr) return PC2D_ERR_CUDA;
-  return pc2d_forward(dtype, input, pars, factor, k0, k1, s0, s1, dl0, dl1, n, channels, height, width, m, output,
-                      hsum, ws, kNoAllocScratchBytes, stream);
+  // nothing on this call's path may allocate (the status word's host mirror
+  // included)
+  t_no_alloc = true;
+  const int st = pc2d_forward(dtype, input, pars, factor, k0, k1, s0, s1, dl0, dl1, n, channels, height, width, m,
+                              output, hsum, ws, kNoAllocScratchBytes, stream);
+  t_no_alloc = false;
+  return st;
 }

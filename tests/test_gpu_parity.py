@@ -14,6 +14,7 @@ import pytest
 import torch
 
 import oracle
+import paraconv2d_b200  # noqa: F401  (registers torch.ops.ptparaconv2d)
 from cabi_runner import algo, backward, forward
 from paraconv2d_b200 import PC2D_ALGO_AUTO, PC2D_ALGO_SIMT, _lib, workloads
 from pc2d_testutil import (check_grads, check_outputs, check_vs_float64, elementwise_excess, golden_manifest,
@@ -222,15 +223,27 @@ def test_edge_empty_batch_and_m1():
 
 def test_bounded_wait_selftest():
     """A device-side wait on a barrier nothing completes returns by itself
-    and records PC2D_ERR_TIMEOUT; the context stays usable."""
+    and records PC2D_ERR_TIMEOUT; the next call of the op raises it (read from
+    the host mirror of the status word, without synchronising), until the
+    status is cleared; the context stays usable."""
     lib = _lib.cabi()
+    x = torch.rand(1, 3, 8, 8, device="cuda")
+    pars = torch.randn(2 * 4 * 28, device="cuda") * 0.1
+    k = torch.tensor([3, 3], dtype=torch.int)
+    one = torch.tensor([1, 1], dtype=torch.int)
+    ref = torch.ops.ptparaconv2d.forward(x, pars, 1.0, k, one, one)
     assert lib.pc2d_clear_device_status() == 0
     assert lib.pc2d_selftest_bounded_wait(200000, None) == 0
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="PC2D_ERR_TIMEOUT"):
+        torch.ops.ptparaconv2d.forward(x, pars, 1.0, k, one, one)
+    with pytest.raises(RuntimeError, match="PC2D_ERR_TIMEOUT"):
+        torch.ops.ptparaconv2d.backward(torch.ones_like(ref[0]), x, pars, ref[1], 1.0, k, one, one, False)
     assert lib.pc2d_device_status() == _lib.PC2D_ERR_TIMEOUT
     assert lib.pc2d_clear_device_status() == 0
     assert lib.pc2d_device_status() == 0
-    y = torch.ones(4, device="cuda") * 2
-    assert float(y.sum()) == 8.0
+    out = torch.ops.ptparaconv2d.forward(x, pars, 1.0, k, one, one)
+    assert torch.equal(out[0], ref[0]) and torch.equal(out[1], ref[1])
 
 
 def test_no_device_errors_after_suite():
