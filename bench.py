@@ -105,6 +105,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-stack", action="store_true", help="skip the data-parallel stack block")
     ap.add_argument("--stack-steps", type=int, default=20)
+    ap.add_argument("--grad-sum", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: sum the parameter gradient inside the backward over NVLink peer memory "
+                         "(pc2d_backward_sum), or with an NCCL all-reduce after it")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU work of the baseline sample")
     return ap.parse_args()
 
@@ -390,16 +393,38 @@ def bench_layer(args, wl, lib, D, rank, world):
         if st != 0:
             raise RuntimeError(_lib.status_message(st))
 
-    def bwd():
+    def bwd_local(dst):
         st = lib.pc2d_backward(0, gd.data_ptr(), xp.data_ptr(), p.data_ptr(), hsum.data_ptr(), 1.0, L.k, L.k, L.s,
-                               L.s, 1, 1, n, C, H, W, m, 0, dx.data_ptr(), dp.data_ptr(), bwsb.data_ptr(), bws, sptr)
+                               L.s, 1, 1, n, C, H, W, m, 0, dx.data_ptr(), dst.data_ptr(), bwsb.data_ptr(), bws, sptr)
+        if st != 0:
+            raise RuntimeError(_lib.status_message(st))
+
+    # N > 1: the data-parallel step sums the parameter gradient over the
+    # ranks, inside the backward (NVLink peer memory) or with NCCL after it
+    comm, grad_sum = None, None
+    if world > 1:
+        grad_sum = "NCCL all_reduce(SUM) of the parameter gradient after the backward"
+        if args.grad_sum == "peer":
+            from paraconv2d_b200.dp import PeerGradComm
+
+            comm = PeerGradComm(p.numel())
+            grad_sum = ("parameter gradient summed over the ranks inside the backward, over NVLink peer memory "
+                        "(pc2d_backward_sum)")
+
+    def bwd():
+        if comm is None:
+            bwd_local(dp)
+            D.all_reduce(dp)
+            return
+        st = lib.pc2d_backward_sum(comm.comm, 0, gd.data_ptr(), xp.data_ptr(), p.data_ptr(), hsum.data_ptr(), 1.0,
+                                   L.k, L.k, L.s, L.s, 1, 1, n, C, H, W, m, 0, dx.data_ptr(), dp.data_ptr(),
+                                   bwsb.data_ptr(), bws, sptr)
         if st != 0:
             raise RuntimeError(_lib.status_message(st))
 
     for _ in range(args.warmup):
         fwd()
         bwd()
-        D.all_reduce(dp)
     torch.cuda.synchronize()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     D.barrier()
@@ -417,7 +442,6 @@ def bench_layer(args, wl, lib, D, rank, world):
         ev[i][1].record(stream)
         bwd()
         ev[i][2].record(stream)
-        D.all_reduce(dp)
         ev[i][3].record(stream)
     torch.cuda.synchronize()
     D.barrier()
@@ -427,7 +451,6 @@ def bench_layer(args, wl, lib, D, rank, world):
         flush.zero_()
         fwd()
         bwd()
-        D.all_reduce(dp)
     torch.cuda.synchronize()
     lib.pc2d_timing_enable(0)
     ktimes = _lib.kernel_times(KERNELS)
@@ -439,6 +462,16 @@ def bench_layer(args, wl, lib, D, rank, world):
     tot_fwd = D.max(sum(t_fwd))
     tot_bwd = D.max(sum(t_bwd))
     images = n * world * args.steps
+    sum_check = None
+    if comm is not None:
+        # the fused sum against NCCL's all-reduce of this rank's own gradient
+        ref = torch.empty_like(dp)
+        bwd_local(ref)
+        D.all_reduce(ref)
+        bwd()
+        torch.cuda.synchronize()
+        err = float((dp - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+        sum_check = {"max_rel_diff_vs_nccl": D.max(err), "bitwise_equal_here": bool(torch.equal(dp, ref))}
 
     # ---- end to end through the public module, host buffers
     layer = pc.ParaConv2d(L.cin, L.cout, L.k, stride=L.s, padding=L.p).to(dev)
@@ -525,8 +558,9 @@ def bench_layer(args, wl, lib, D, rank, world):
         "value": images / tot_step, "ms_per_step": 1e3 * tot_step / args.steps,
         "fwd_images_per_s": images / tot_fwd, "fwd_ms": 1e3 * mean_fwd, "bwd_ms": 1e3 * mean_bwd,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * launches_per_step(ktimes, args.steps),
+        "gpu_launches": args.steps * (launches_per_step(ktimes, args.steps) + (1 if comm is not None else 0)),
         "roofline": roofline, "clock": clk, "algo": {0: "auto", 1: "simt", 2: "tc"}[lib.pc2d_get_algo()],
+        "grad_sum": grad_sum, "grad_sum_check": sum_check, "comm": comm,
     }
 
 
@@ -730,9 +764,12 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "config": cfg,
             "fwd_images_per_s": r["fwd_images_per_s"], "fwd_ms": r["fwd_ms"], "bwd_ms": r["bwd_ms"],
             "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "roofline": r["roofline"], "cpu_baseline": cpu,
-            "clocks": r["clock"].summary(), "algo": r["algo"], "dp_step": stack,
+            "clocks": r["clock"].summary(), "algo": r["algo"], "grad_sum": r["grad_sum"],
+            "grad_sum_check": r["grad_sum_check"], "dp_step": stack,
         }
         print(json.dumps(line), flush=True)
+    if r["comm"] is not None:
+        r["comm"].close()
     D.close()
     return 0
 

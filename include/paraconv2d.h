@@ -156,6 +156,38 @@ int pc2d_backward_interior(int dtype, const void *grad, const void *input, const
                            void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes,
                            void *stream);
 
+/* ---------------------------------------------------------------------------
+ * Data-parallel training: the backward pass with the parameter gradient
+ * summed over the ranks (one process per GPU, up to 8 GPUs of one node with
+ * peer access), over NVLink peer memory instead of a separate all-reduce.
+ * The reference has no multi-GPU path; this replaces the all-reduce (SUM) of
+ * pars.grad after the backward in a data-parallel loop.
+ *
+ * Setup, once per process group (allocates: do it before any stream capture):
+ *   pc2d_comm_create   -> this rank's exchange buffer (cudaMalloc) and an IPC
+ *                         handle of pc2d_comm_handle_bytes() bytes;
+ *   (the caller gathers every rank's handle, in rank order, by any channel,
+ *    e.g. torch.distributed.all_gather_object)
+ *   pc2d_comm_connect  -> maps every peer's buffer;
+ *   pc2d_comm_destroy  -> unmaps and frees (after every rank's last call has
+ *                         completed: a barrier first).
+ * pc2d_backward_sum: as pc2d_backward (fp32), with parsgrad receiving the sum
+ * of all ranks' parameter gradients, the same bits on every rank (fixed rank
+ * order).  Every rank must make the same sequence of pc2d_backward_sum calls
+ * on its communicator (like a collective); the calls of one communicator go
+ * on one stream.  A rank that waits longer than 2 s for its peers records
+ * PC2D_ERR_TIMEOUT in the device status (see above) and returns its own
+ * gradient. */
+typedef struct pc2d_comm pc2d_comm;
+size_t pc2d_comm_handle_bytes(void);
+int pc2d_comm_create(int rank, int world, size_t max_params, pc2d_comm **comm, void *handle_out);
+int pc2d_comm_connect(pc2d_comm *comm, const void *handles);
+int pc2d_comm_destroy(pc2d_comm *comm);
+int pc2d_backward_sum(pc2d_comm *comm, int dtype, const void *grad, const void *input, const void *pars,
+                      const void *hsum, double factor, int k0, int k1, int s0, int s1, int dl0, int dl1,
+                      int n, int channels, int height, int width, int m, int skip_input_grad,
+                      void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes, void *stream);
+
 /* Human-readable name of a pc2d_status. */
 const char *pc2d_status_string(int status);
 

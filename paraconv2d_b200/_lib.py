@@ -80,6 +80,11 @@ def cabi() -> ctypes.CDLL:
             "pc2d_backward": ([I, P, P, P, P, D] + [I] * 12 + [P, P, P, S, P], I),
             "pc2d_backward_interior": ([I, P, P, P, P, D] + [I] * 16 + [D, P, P, P, S, P], I),
             "pc2d_pad_scale": ([I, P] + [I] * 8 + [D, P, P], I),
+            "pc2d_comm_handle_bytes": ([], S),
+            "pc2d_comm_create": ([I, I, S, ctypes.POINTER(P), P], I),
+            "pc2d_comm_connect": ([P, P], I),
+            "pc2d_comm_destroy": ([P], I),
+            "pc2d_backward_sum": ([P, I, P, P, P, P, D] + [I] * 12 + [P, P, P, S, P], I),
             "pc2d_status_string": ([I], ctypes.c_char_p),
             "pc2d_last_error": ([], ctypes.c_char_p),
             "pc2d_device_status": ([], I),

@@ -9,6 +9,7 @@ depend on the number of ranks.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Iterable, List, Optional
 
 import torch
@@ -99,3 +100,44 @@ class GradAllReduce:
         for h in self._hooks:
             h.remove()
         self._hooks.clear()
+
+
+class PeerGradComm:
+    """The communicator of ``pc2d_backward_sum`` (include/paraconv2d.h) for
+    this rank: each rank's exchange buffer mapped by every other rank over
+    CUDA IPC, so that the backward pass itself sums the parameter gradient
+    over the ranks (NVLink peer loads, fixed rank order), with no all-reduce
+    after it.  One process per GPU, at most 8 GPUs of one node.
+
+    Creating it is collective over ``group`` (the IPC handles are exchanged
+    with ``all_gather_object``); so is ``close``, which waits for every rank
+    before unmapping.  ``max_params`` bounds the parameter count of the
+    layers it serves."""
+
+    def __init__(self, max_params: int, group: Optional[dist.ProcessGroup] = None):
+        from ._lib import cabi, status_message
+
+        self._lib = cabi()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        nb = self._lib.pc2d_comm_handle_bytes()
+        handle = (ctypes.c_char * nb)()
+        comm = ctypes.c_void_p()
+        st = self._lib.pc2d_comm_create(self.rank, self.world, int(max_params), ctypes.byref(comm), handle)
+        if st != 0:
+            raise RuntimeError(status_message(st))
+        self.comm = comm
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, bytes(handle), group=group)
+        blob = b"".join(gathered)
+        st = self._lib.pc2d_comm_connect(self.comm, blob)
+        if st != 0:
+            raise RuntimeError(status_message(st))
+
+    def close(self):
+        if self.comm is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            self._lib.pc2d_comm_destroy(self.comm)
+            self.comm = None

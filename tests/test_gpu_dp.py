@@ -103,3 +103,62 @@ def test_two_rank_gradient_equals_full_batch(bucketed, tmp_path):
             assert e <= 1.0, f"rank {r} layer {i}: all-reduced gradient differs from the full batch by {e:.3g}x"
             off += g.numel()
         assert torch.isfinite(got).all()
+
+
+def _peer_worker(rank, world, port, outdir):
+    import torch.distributed as dist
+
+    from cabi_runner import backward, forward
+    from paraconv2d_b200 import _lib
+    from paraconv2d_b200.dp import PeerGradComm
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        lib = _lib.cabi()
+        gen = torch.Generator().manual_seed(100 + rank)  # each rank its own shard
+        n, C, H, W, m, k = 4, 16, 18, 18, 24, 3
+        x = (torch.rand(n, C, H, W, generator=gen) * 2 - 1).to(dev)
+        pars = (torch.randn(2 * m * (C * k * k + 1), generator=torch.Generator().manual_seed(7)) * 0.05).to(dev)
+        out, hsum = forward(x, pars, 1.0, k)
+        g = torch.randn(out.shape, generator=gen).to(dev)
+        comm = PeerGradComm(pars.numel())
+        wsb = lib.pc2d_backward_workspace_size(0, n, C, H, W, m, k, k, 1, 1, 1, 1, 0)
+        ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream().cuda_stream
+        results = []
+        for _ in range(3):  # both exchange slots, then the first again
+            ref_dx, ref = backward(g, x, pars, hsum, 1.0, k)
+            dist.all_reduce(ref)
+            dx = torch.empty_like(x)
+            dp = torch.empty_like(pars)
+            st = lib.pc2d_backward_sum(comm.comm, 0, g.data_ptr(), x.data_ptr(), pars.data_ptr(), hsum.data_ptr(),
+                                       1.0, k, k, 1, 1, 1, 1, n, C, H, W, m, 0, dx.data_ptr(), dp.data_ptr(),
+                                       ws.data_ptr(), wsb, stream)
+            assert st == 0, _lib.status_message(st)
+            torch.cuda.synchronize()
+            results.append((torch.equal(dp, ref), torch.equal(dx, ref_dx)))
+        assert lib.pc2d_device_status() == 0
+        comm.close()
+        torch.save({"results": results, "dp": dp.cpu()}, os.path.join(outdir, f"peer{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_sum_equals_nccl_allreduce(tmp_path):
+    """pc2d_backward_sum on two GPUs: the parameter gradient summed over
+    NVLink peer memory equals NCCL's all-reduce of the ranks' own gradients
+    bit for bit (two addends: both round the exact sum once), on both ranks
+    and over three calls (both exchange slots); the input gradient is the
+    rank's own."""
+    mp.start_processes(_peer_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    r0 = torch.load(os.path.join(tmp_path, "peer0.pt"))
+    r1 = torch.load(os.path.join(tmp_path, "peer1.pt"))
+    assert all(a and b for a, b in r0["results"] + r1["results"])
+    assert torch.equal(r0["dp"], r1["dp"])
