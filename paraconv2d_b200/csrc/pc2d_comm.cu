@@ -9,14 +9,18 @@
 // of that layer's 0.41 ms step.  Here the backward's own fixed-order reduction
 // writes the rank's gradient into an exchange buffer that every rank has
 // mapped (CUDA IPC, one process per GPU), and one more small kernel sums it:
+//   - it is a programmatic dependent of the reduction (its launch overlaps
+//     the reduction; griddepcontrol.wait holds it until the gradient is
+//     complete);
 //   - block b of the sum kernel owns a slice of the gradient; it publishes
-//     flag[b] = epoch in its own buffer (the gradient is complete and
-//     visible: the reduction that wrote it finished before this kernel, and
-//     peers read this GPU's memory through its L2), then waits until the
-//     same flag of every peer has reached the epoch (a bounded spin on peer
-//     memory, acquire at system scope), then loads the slice of every rank
-//     (all ranks' loads in flight together) and adds them in rank order
-//     (fp64), writing the caller's gradient array;
+//     "slice b of epoch e is ready" by a posted store into every PEER's
+//     buffer (flag[rank][b] there), then waits until flag[q][b] in its OWN
+//     buffer has reached the epoch for every peer q (a bounded spin on local
+//     memory, acquire at system scope: a flag arrives after one NVLink
+//     crossing, no round trip per poll);
+//   - then every thread loads one 16-byte vector of the slice from every rank
+//     (all ranks' loads in flight together: one round trip) and adds them in
+//     rank order (fp64), writing the caller's gradient array;
 //   - the grid is no larger than what is resident at once, so every block of
 //     every rank runs at the same time and no block waits on one that cannot
 //     be scheduled;
@@ -24,7 +28,8 @@
 //     most one call ahead of a peer (its next call waits on the peer's flags
 //     of this call), so it never overwrites a slot a peer is still reading.
 // Every rank adds the same values in the same order: the summed gradient is
-// bitwise identical on all ranks.  Loads only: no multicast, no NVLS.
+// bitwise identical on all ranks.  Loads and stores only: no multicast, no
+// NVLS.
 #include <algorithm>
 #include <cstring>
 
@@ -35,12 +40,11 @@ namespace {
 
 constexpr int kMaxRanks = 8;
 constexpr int kSumThreads = 256;
-constexpr int kSumBlocks = 64;   // (at most one per SM: all resident)
 constexpr uint64_t kPeerWaitNs = 2000000000ull;  // 2 s
 
 struct PeerPtrs {
-  float *data[kMaxRanks];      // [2 slots][max_params] per rank
-  unsigned *flags[kMaxRanks];  // [nblocks] per rank
+  float *data[kMaxRanks];      // [2 slots][stride] per rank
+  unsigned *flags[kMaxRanks];  // [kMaxRanks sources][nblocks] per rank
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
@@ -57,22 +61,32 @@ __device__ __forceinline__ uint64_t now_ns() {
   return t;
 }
 
+// Grid: nblocks blocks of kSumThreads; block b sums vectors
+// [b * kSumThreads * vpt, (b + 1) * kSumThreads * vpt) of the gradient, 4
+// floats each (npars need not be a multiple of 4: the last vector is summed
+// element by element).  stride (floats between the two slots) is a multiple
+// of 4, so every vector is 16-byte aligned.  own_flags is
+// peers.flags[rank], passed on its own: indexing the parameter array with the
+// run-time rank would copy it to local memory.
 __global__ void __launch_bounds__(kSumThreads) peer_sum_kernel(PeerPtrs peers, int world, int rank, unsigned epoch,
-                                                               int slot, int64_t max_params, int64_t npars,
-                                                               float *__restrict__ out, int *status) {
-  const int64_t chunk = ((npars + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
-  const int64_t lo = (int64_t)blockIdx.x * chunk, hi = std::min<int64_t>(npars, lo + chunk);
+                                                               int slot, int64_t stride, int64_t npars, int vpt,
+                                                               const unsigned *own_flags, float *__restrict__ out,
+                                                               int *status) {
   __shared__ int s_ok;
+  // the rank's own slice is written by the reduction this grid depends on
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
-    // this rank's slice is complete and visible: the reduction that wrote it
-    // is an earlier kernel on the stream, and peers read this GPU's memory
-    // through its L2.  Publish it, then wait for every peer's.
-    st_relaxed_sys(peers.flags[rank] + blockIdx.x, epoch);
+    // publish: the slot is complete (fence: the reduction's writes before the
+    // flag, at system scope), into every peer's buffer
+    __threadfence_system();
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q)
+      if (q < world && q != rank) st_relaxed_sys(peers.flags[q] + (size_t)rank * gridDim.x + blockIdx.x, epoch);
     int ok = 1;
     const uint64_t t0 = now_ns();
     for (int q = 0; q < world && ok; ++q) {
       if (q == rank) continue;
-      while ((int)(ld_acquire_sys(peers.flags[q] + blockIdx.x) - epoch) < 0) {
+      while ((int)(ld_acquire_sys(own_flags + (size_t)q * gridDim.x + blockIdx.x) - epoch) < 0) {
         if (now_ns() - t0 > kPeerWaitNs) {
           ok = 0;
           break;
@@ -84,17 +98,35 @@ __global__ void __launch_bounds__(kSumThreads) peer_sum_kernel(PeerPtrs peers, i
   }
   __syncthreads();
   if (!s_ok) return;
-  const int64_t base = (int64_t)slot * max_params;
-  for (int64_t e = lo + threadIdx.x; e < hi; e += kSumThreads) {
-    // every rank's value in flight at once, then the sum in rank order
-    float v[kMaxRanks];
-#pragma unroll
-    for (int q = 0; q < kMaxRanks; ++q) v[q] = q < world ? __ldcv(peers.data[q] + base + e) : 0.f;
-    double acc = 0.0;
+  const int64_t base = (int64_t)slot * stride;
+  const int64_t nvec = (npars + 3) / 4;
+  const int64_t v0 = (int64_t)blockIdx.x * kSumThreads * vpt;
+  for (int u = 0; u < vpt; ++u) {
+    const int64_t v = v0 + (int64_t)u * kSumThreads + threadIdx.x;
+    if (v >= nvec) break;
+    // every rank's vector in flight at once, then the sum in rank order
+    float4 x[kMaxRanks];
 #pragma unroll
     for (int q = 0; q < kMaxRanks; ++q)
-      if (q < world) acc += (double)v[q];
-    out[e] = (float)acc;
+      x[q] = q < world ? __ldcv(reinterpret_cast<const float4 *>(peers.data[q] + base) + v) : make_float4(0, 0, 0, 0);
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q)
+      if (q < world) {
+        a0 += (double)x[q].x;
+        a1 += (double)x[q].y;
+        a2 += (double)x[q].z;
+        a3 += (double)x[q].w;
+      }
+    const int64_t e = 4 * v;
+    if (e + 4 <= npars && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+      reinterpret_cast<float4 *>(out)[v] = make_float4((float)a0, (float)a1, (float)a2, (float)a3);
+    } else {
+      out[e] = (float)a0;
+      if (e + 1 < npars) out[e + 1] = (float)a1;
+      if (e + 2 < npars) out[e + 2] = (float)a2;
+      if (e + 3 < npars) out[e + 3] = (float)a3;
+    }
   }
 }
 
@@ -106,16 +138,18 @@ using namespace pc2d;
 struct pc2d_comm {
   int rank = 0, world = 1, dev = -1;
   size_t max_params = 0;
-  int nblocks = 0;
+  size_t stride = 0;  // floats per exchange slot: max_params rounded up to 4
+  int nblocks = 0;    // sum kernel grid (fixed: the flags are per block)
+  int vpt = 1;        // 4-float vectors per thread of the sum kernel
   unsigned epoch = 0;
-  void *own = nullptr;  // cudaMalloc'd: [2][max_params] floats, then [nblocks] flags
+  void *own = nullptr;  // cudaMalloc'd: [2][stride] floats, then [world][nblocks] flags
   void *peer_base[kMaxRanks] = {};
   PeerPtrs ptrs = {};
   bool connected = false;
 };
 
 namespace {
-size_t flags_offset(size_t max_params) { return align_up(2 * max_params * sizeof(float), 256); }
+size_t flags_offset(size_t stride) { return align_up(2 * stride * sizeof(float), 256); }
 }  // namespace
 
 extern "C" {
@@ -130,6 +164,7 @@ int pc2d_comm_create(int rank, int world, size_t max_params, pc2d_comm **comm, v
   c->rank = rank;
   c->world = world;
   c->max_params = max_params;
+  c->stride = align_up(max_params, 4);
   if (cudaGetDevice(&c->dev) != cudaSuccess) {
     delete c;
     set_last_error("pc2d_comm_create: no current device");
@@ -140,9 +175,12 @@ int pc2d_comm_create(int rank, int world, size_t max_params, pc2d_comm **comm, v
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, peer_sum_kernel, kSumThreads, 0) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
-  // every block resident at once (see the file comment)
-  c->nblocks = std::max(1, std::min(kSumBlocks, sms * per_sm));
-  const size_t bytes = flags_offset(max_params) + (size_t)c->nblocks * sizeof(unsigned);
+  // every block resident at once (see the file comment); one vector per
+  // thread when the gradient fits such a grid
+  const int64_t nvec = (int64_t)c->stride / 4;
+  c->nblocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(nvec, kSumThreads), (int64_t)sms * per_sm));
+  c->vpt = ceil_div(nvec, (int64_t)c->nblocks * kSumThreads);
+  const size_t bytes = flags_offset(c->stride) + (size_t)world * c->nblocks * sizeof(unsigned);
   cudaError_t e = cudaMalloc(&c->own, bytes);
   if (e == cudaSuccess) e = cudaMemset(c->own, 0, bytes);
   cudaIpcMemHandle_t h;
@@ -166,7 +204,7 @@ int pc2d_comm_connect(pc2d_comm *c, const void *handles) {
     return PC2D_ERR_INVALID_ARGUMENT;
   }
   const char *hb = static_cast<const char *>(handles);
-  const size_t fo = flags_offset(c->max_params);
+  const size_t fo = flags_offset(c->stride);
   for (int q = 0; q < c->world; ++q) {
     void *base = c->own;
     if (q != c->rank) {
@@ -225,7 +263,7 @@ int pc2d_backward_sum(pc2d_comm *c, int dtype, const void *grad, const void *inp
   }
   const unsigned epoch = c->epoch + 1;
   const int slot = (int)(epoch & 1);
-  float *mine = c->ptrs.data[c->rank] + (size_t)slot * c->max_params;
+  float *mine = c->ptrs.data[c->rank] + (size_t)slot * c->stride;
   // this rank's gradient, into its exchange slot
   int st = pc2d_backward(dtype, grad, input, pars, hsum, factor, k0, k1, s0, s1, dl0, dl1, n, channels, height, width,
                          m, skip_input_grad, inputgrad, mine, workspace, workspace_bytes, stream);
@@ -237,8 +275,19 @@ int pc2d_backward_sum(pc2d_comm *c, int dtype, const void *grad, const void *inp
     return PC2D_ERR_CUDA;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  peer_sum_kernel<<<c->nblocks, kSumThreads, 0, s>>>(c->ptrs, c->world, c->rank, epoch, slot, (int64_t)c->max_params,
-                                                      npars, static_cast<float *>(parsgrad), status);
+  // a programmatic dependent of the reduction that wrote the slot
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c->nblocks);
+  cfg.blockDim = dim3(kSumThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, peer_sum_kernel, c->ptrs, c->world, c->rank, epoch, slot,
+                                     (int64_t)c->stride, npars, c->vpt, (const unsigned *)c->ptrs.flags[c->rank],
+                                     static_cast<float *>(parsgrad), status));
   PC2D_LAUNCH_CHECK("peer_sum_kernel");
   c->epoch = epoch;
   return PC2D_OK;

@@ -119,7 +119,7 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   // 16-byte boundary at or below the chunk's first element), at most 256.
   c.tma = (p.HW % 4 == 0 && c.PSw <= 256 && (int64_t)p.n * p.C < ((int64_t)1 << 31)) ? 1 : 0;
   c.kst = kStages;
-  const size_t need = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256) * 4 + 28 * 8 + 64;
+  const size_t need = 1024 + (size_t)kStages * (c.bstage + c.hstage) + (size_t)kStages * (64 + 256 + 32) * 4 + 28 * 8 + 64;
   if (need > (size_t)kSmemLimit) c.halo = 0;  // gather from global memory instead
   if (!c.halo) {
     c.hstage = 0;
@@ -133,7 +133,7 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   // (with the halo path, two B and halo stages when three leave no room)
   if (p.PQ % 4 == 0 && p.PQ >= kChunk && (int64_t)p.n * p.m < ((int64_t)1 << 31)) {
     for (int kst = kStages; kst >= (c.halo ? 2 : kStages); --kst) {
-      const size_t need2 = 1024 + (size_t)kst * (c.bstage + c.hstage) + (size_t)kst * (64 + 256) * 4 + 28 * 8 + 64;
+      const size_t need2 = 1024 + (size_t)kst * (c.bstage + c.hstage) + (size_t)kst * (64 + 256 + 32) * 4 + 28 * 8 + 64;
       if (need2 + 2 * 2 * 8192 <= (size_t)kSmemLimit) {
         c.atma = 1;
         c.tbytes = 2 * 2 * 8192;
@@ -147,7 +147,7 @@ WgCfg wg_cfg(const Problem &p, int sms) {
 
 inline size_t wg_smem_bytes(const WgCfg &c) {
   size_t s = 1024 + (size_t)c.kst * (c.bstage + c.hstage) + c.tbytes + (size_t)c.kst * 64 * 4 +
-             (size_t)c.kst * 256 * 4 + 28 * 8 + 64;
+             (size_t)c.kst * (256 + 32) * 4 + 28 * 8 + 64;
   return std::max<size_t>(s, kMinSmem);
 }
 
@@ -157,10 +157,29 @@ struct ChunkGeo {
   int pq0, npx, ir0, rows;
 };
 
-__device__ __forceinline__ ChunkGeo chunk_geo(const Problem &p, const WgCfg &c, int64_t gc) {
+// Chunk gc = image n, chunk ci of that image.  The roles walk the chunks of
+// a segment in order and step (n, ci) instead of dividing gc per chunk.
+struct ChunkPos {
+  int64_t n;
+  int ci;
+};
+__device__ __forceinline__ ChunkPos chunk_pos(const WgCfg &c, int64_t gc) {
+  ChunkPos t;
+  t.n = gc / c.cpi;
+  t.ci = (int)(gc - t.n * c.cpi);
+  return t;
+}
+__device__ __forceinline__ void chunk_next(const WgCfg &c, ChunkPos &t) {
+  if (++t.ci == c.cpi) {
+    t.ci = 0;
+    ++t.n;
+  }
+}
+
+__device__ __forceinline__ ChunkGeo chunk_geo(const Problem &p, const ChunkPos &t) {
   ChunkGeo g;
-  g.n = gc / c.cpi;
-  g.pq0 = (int)(gc - g.n * c.cpi) * kChunk;
+  g.n = t.n;
+  g.pq0 = t.ci * kChunk;
   g.npx = min(kChunk, (int)p.PQ - g.pq0);
   const int oya = g.pq0 / p.Q, oyb = (g.pq0 + g.npx - 1) / p.Q;
   g.ir0 = oya * p.s0;
@@ -188,7 +207,8 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   uint8_t *sT = sH + (size_t)KST * c.hstage;                      // 2 x [g tile 8 KB | hsum tile 8 KB]
   int *lead = reinterpret_cast<int *>(sT + c.tbytes);                 // [KST][64]
   int *roffs = lead + KST * 64;                                    // [KST][256]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(roffs + KST * 256);
+  int *pofs = roffs + KST * 256;  // [KST][32]: pixel offsets in the staged rows (-1: past the chunk)
+  uint64_t *bars = reinterpret_cast<uint64_t *>(pofs + KST * 32);
   uint64_t *a_full = bars, *a_empty = bars + 3, *b_full = bars + 6, *b_empty = bars + 9;
   uint64_t *d_full = bars + 12, *d_empty = bars + 13, *final_bar = bars + 14;
   uint64_t *h_full = bars + 15, *h_empty = bars + 18;
@@ -245,15 +265,15 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       const bool rvalid = r < 2 * c.JM && j < p.m;
       float rowsum = 0.f;
       const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
-      for (int64_t gc = g0; gc < g1; ++gc, ++it) {
-        const int64_t n = gc / c.cpi;
-        const int pq0 = (int)(gc - n * c.cpi) * kChunk;
+      ChunkPos cp = chunk_pos(c, g0), ca = chunk_pos(c, g0 + kAhead);
+      for (int64_t gc = g0; gc < g1; ++gc, ++it, chunk_next(c, cp), chunk_next(c, ca)) {
+        const int64_t n = cp.n;
+        const int pq0 = cp.ci * kChunk;
         const int npx = min(kChunk, (int)p.PQ - pq0);
         // this row kAhead chunks ahead: start bringing it into L2 now (one
         // thread holds one 128-byte row of a chunk)
         if (rvalid && gc + kAhead < g1) {
-          const int64_t na = (gc + kAhead) / c.cpi;
-          const int64_t offa = (na * p.m + j) * p.PQ + (int)(gc + kAhead - na * c.cpi) * kChunk;
+          const int64_t offa = (ca.n * p.m + j) * p.PQ + ca.ci * kChunk;
           prefetch_l2(grad + offa);
           if (w == 0) prefetch_l2(hsum + offa);
         }
@@ -374,11 +394,8 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         }
       }
       const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
-      for (int64_t gc = g0; gc < g1; ++gc, ++it) {
-        const ChunkGeo cg = chunk_geo(p, c, gc);
-        const int pq = cg.pq0 + lane;
-        const bool pvalid = lane < cg.npx;
-        const int oy = pq / p.Q, ox = pq - (pq / p.Q) * p.Q;
+      ChunkPos cp = chunk_pos(c, g0);
+      for (int64_t gc = g0; gc < g1; ++gc, ++it, chunk_next(c, cp)) {
         const uint32_t st = it % KST, ph = (it / KST) & 1;
         if (c.halo && !warp_wait(&h_full[st], ph, abort_flag)) {
           ok = false;
@@ -398,15 +415,12 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           const int g = lane & 7, rr = lane >> 3;
           const uint32_t halo = smem_u32(sH + (size_t)st * c.hstage);
           const int *ro = roffs + st * 256 + bw * 32;
-          int poff[4];
+          // offsets of pixels 4g .. 4g+3 in the staged rows (the loader's)
+          const int4 po4 = lds_v4s32(smem_u32(pofs + st * 32 + 4 * g));
+          const int poff[4] = {po4.x, po4.y, po4.z, po4.w};
           bool pv[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int px = 4 * g + j, q = cg.pq0 + px;
-            const int qy = q / p.Q, qx = q - qy * p.Q;
-            pv[j] = px < cg.npx;
-            poff[j] = (qy * p.s0 - cg.ir0) * p.W + qx * p.s1;
-          }
+          for (int j = 0; j < 4; ++j) pv[j] = poff[j] >= 0;
           const uint32_t cbyte = (uint32_t)((g ^ bw) << 4);
           int o[8];
 #pragma unroll
@@ -435,6 +449,10 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         } else {
           // lane = pixel; row kl = bw + 8*i gathered from global memory (lane
           // i holds the input offset of row bw + 8*i of the window range)
+          const ChunkGeo cg = chunk_geo(p, cp);
+          const int pq = cg.pq0 + lane;
+          const bool pvalid = lane < cg.npx;
+          const int oy = pq / p.Q, ox = pq - oy * p.Q;
           const int64_t pbase = cg.n * p.CHW + (int64_t)oy * p.s0 * p.W + (int64_t)ox * p.s1;
           float v[32];
 #pragma unroll
@@ -517,12 +535,23 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         }
         const int nch = (int)(std::min<int64_t>(kbase + c.NR, p.d) - 1) / p.T - clo + 1;
         const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
-        for (int64_t gc = g0; gc < g1; ++gc, ++it) {
-          const ChunkGeo cg = chunk_geo(p, c, gc);
+        ChunkPos cp = chunk_pos(c, g0);
+        for (int64_t gc = g0; gc < g1; ++gc, ++it, chunk_next(c, cp)) {
+          const ChunkGeo cg = chunk_geo(p, cp);
           const uint32_t st = it % KST, ph = (it / KST) & 1;
           if (!warp_wait(&h_empty[st], ph ^ 1, abort_flag)) {
             ok = false;
             break;
+          }
+          {
+            // lane = pixel of the chunk: its offset from the first staged
+            // input row (published with the row offsets below)
+            int po = -1;
+            if (lane < cg.npx) {
+              const int q = cg.pq0 + lane, qy = q / p.Q;
+              po = (qy * p.s0 - cg.ir0) * p.W + (q - qy * p.Q) * p.s1;
+            }
+            pofs[st * 32 + lane] = po;
           }
           uint8_t *hb = sH + (size_t)st * c.hstage;
           if (c.tma) {
@@ -592,15 +621,16 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         const int64_t seg = item / per;
         const int mb = (int)((item - seg * per) % c.nmb);
         const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
-        for (int64_t gc = g0; gc < g1; ++gc, ++it) {
+        ChunkPos cp = chunk_pos(c, g0);
+        for (int64_t gc = g0; gc < g1; ++gc, ++it, chunk_next(c, cp)) {
           const uint32_t ts = it & 1, tph = (it >> 1) & 1;
           if (!warp_wait(&t_empty[ts], tph ^ 1, abort_flag)) {
             ok = false;
             break;
           }
           if (lane == 0) {
-            const int64_t n = gc / c.cpi;
-            const int pq0 = (int)(gc - n * c.cpi) * kChunk;
+            const int64_t n = cp.n;
+            const int pq0 = cp.ci * kChunk;
             uint8_t *tb = sT + (size_t)ts * 16384;
             const int ty = (int)(n * p.m + mb * c.JM);
             mbar_arrive_expect_tx(&t_full[ts], (uint32_t)(2 * c.JM * 128));
@@ -699,6 +729,9 @@ tc_wgrad_finalize(const float *__restrict__ part, const float *__restrict__ sums
   // launched as a programmatic dependent of the parameter-gradient kernel:
   // its partials are complete and visible only after this wait
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // a programmatic dependent of this grid (the data-parallel peer sum) may
+  // start now: it waits for this grid's completion before it reads anything
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int j = blockIdx.y;
   const int kx = threadIdx.x % kFinK, q = threadIdx.x / kFinK;
   const int64_t k = (int64_t)blockIdx.x * kFinK + kx;
