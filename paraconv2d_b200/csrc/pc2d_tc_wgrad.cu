@@ -76,6 +76,7 @@ struct WgCfg {
   int atma;         // 1: a chunk's g and hsum rows are two 2-D tensor copies [JM][32] (128-byte swizzled)
   int kst;          // B / halo stages in flight (3, or 2 to make room for the A tiles)
   uint32_t tbytes;  // shared bytes of those tiles: 2 stages x (g, hsum) x 8 KB, or 0
+  int dqy, dqx;     // a chunk's 32 pixels as output rows and columns: 32 = dqy * Q + dqx
 };
 
 WgCfg wg_cfg(const Problem &p, int sms) {
@@ -86,6 +87,8 @@ WgCfg wg_cfg(const Problem &p, int sms) {
   c.NR = (ceil_div(p.d, c.nNR) + 15) / 16 * 16;
   c.cpi = ceil_div(p.PQ, kChunk);
   c.chunks = (int64_t)p.n * c.cpi;
+  c.dqy = kChunk / (int)std::max<int64_t>(1, p.Q);
+  c.dqx = kChunk - c.dqy * (int)std::max<int64_t>(1, p.Q);
   const int64_t per = (int64_t)c.nNR * c.nmb;
   // Segment length: the one whose critical path (rounds of items per SM x
   // chunks per item, plus a per-item cost of ~2 chunks for the drain and
@@ -176,6 +179,33 @@ __device__ __forceinline__ void chunk_next(const WgCfg &c, ChunkPos &t) {
   }
 }
 
+// Output pixel pq0 + lane of the chunk at t as (row qy, column qx); stepped
+// with the chunk: +32 pixels = +dqy rows, +dqx columns (one carry at most,
+// as dqx < Q), or back to pixel lane of the next image.
+struct LanePix {
+  int qy, qx;
+};
+__device__ __forceinline__ LanePix lane_pix(const Problem &p, const ChunkPos &t, int lane) {
+  LanePix v;
+  const int q = t.ci * kChunk + lane;
+  v.qy = q / (int)p.Q;
+  v.qx = q - v.qy * (int)p.Q;
+  return v;
+}
+__device__ __forceinline__ void chunk_next(const Problem &p, const WgCfg &c, ChunkPos &t, LanePix &v, int lane) {
+  chunk_next(c, t);
+  if (t.ci == 0) {
+    v = lane_pix(p, t, lane);
+  } else {
+    v.qy += c.dqy;
+    v.qx += c.dqx;
+    if (v.qx >= (int)p.Q) {
+      v.qx -= (int)p.Q;
+      ++v.qy;
+    }
+  }
+}
+
 __device__ __forceinline__ ChunkGeo chunk_geo(const Problem &p, const ChunkPos &t) {
   ChunkGeo g;
   g.n = t.n;
@@ -206,7 +236,7 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
   uint8_t *sH = base + (size_t)KST * c.bstage;                     // KST x hstage
   uint8_t *sT = sH + (size_t)KST * c.hstage;                      // 2 x [g tile 8 KB | hsum tile 8 KB]
   int *lead = reinterpret_cast<int *>(sT + c.tbytes);                 // [KST][64]
-  int *roffs = lead + KST * 64;                                    // [KST][256]
+  int *roffs = lead + KST * 64;                                    // [KST][8 warps][32 slots]
   int *pofs = roffs + KST * 256;  // [KST][32]: pixel offsets in the staged rows (-1: past the chunk)
   uint64_t *bars = reinterpret_cast<uint64_t *>(pofs + KST * 32);
   uint64_t *a_full = bars, *a_empty = bars + 3, *b_full = bars + 6, *b_empty = bars + 9;
@@ -519,11 +549,13 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
         const int nr = (int)((item - seg * per) / c.nmb);
         const int64_t kbase = (int64_t)nr * c.NR;
         const int clo = (int)(kbase / p.T);
-        // (channel - clo, tap offset) of the window rows this lane writes
+        // (channel - clo, tap offset) of the window rows this lane writes:
+        // table entry e*32 + lane = slot `lane` of B-producer warp e = row
+        // e + 8*lane (consecutive lanes store consecutive words)
         int rc[8], rt[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int kl = lane + 32 * e;
+          const int kl = e + kBWarps * lane;
           const int64_t k = kbase + kl;
           rc[e] = -1;
           rt[e] = 0;
@@ -533,26 +565,31 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
             rt[e] = tap_row(p, tap) * p.W + tap_col(p, tap);
           }
         }
+        // row offsets in a stage without the chunk's lead (a row past the
+        // range stays negative whatever the lead)
+        int rb[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) rb[e] = rc[e] >= 0 ? rc[e] * c.PSw + rt[e] : -(1 << 30);
         const int nch = (int)(std::min<int64_t>(kbase + c.NR, p.d) - 1) / p.T - clo + 1;
         const int64_t g0 = seg * c.SEG, g1 = std::min<int64_t>(c.chunks, g0 + c.SEG);
         ChunkPos cp = chunk_pos(c, g0);
-        for (int64_t gc = g0; gc < g1; ++gc, ++it, chunk_next(c, cp)) {
-          const ChunkGeo cg = chunk_geo(p, cp);
+        LanePix lp = lane_pix(p, cp, lane);
+        for (int64_t gc = g0; gc < g1; ++gc, ++it, chunk_next(p, c, cp, lp, lane)) {
+          ChunkGeo cg;
+          cg.n = cp.n;
+          cg.pq0 = cp.ci * kChunk;
+          cg.npx = min(kChunk, (int)p.PQ - cg.pq0);
+          const int oya = __shfl_sync(0xffffffffu, lp.qy, 0), oyb = __shfl_sync(0xffffffffu, lp.qy, cg.npx - 1);
+          cg.ir0 = oya * p.s0;
+          cg.rows = (oyb - oya) * p.s0 + (p.k0 - 1) * p.dl0 + 1;
           const uint32_t st = it % KST, ph = (it / KST) & 1;
           if (!warp_wait(&h_empty[st], ph ^ 1, abort_flag)) {
             ok = false;
             break;
           }
-          {
-            // lane = pixel of the chunk: its offset from the first staged
-            // input row (published with the row offsets below)
-            int po = -1;
-            if (lane < cg.npx) {
-              const int q = cg.pq0 + lane, qy = q / p.Q;
-              po = (qy * p.s0 - cg.ir0) * p.W + (q - qy * p.Q) * p.s1;
-            }
-            pofs[st * 32 + lane] = po;
-          }
+          // lane = pixel of the chunk: its offset from the first staged input
+          // row (published with the row offsets below)
+          pofs[st * 32 + lane] = lane < cg.npx ? (lp.qy * p.s0 - cg.ir0) * p.W + lp.qx * p.s1 : -1;
           uint8_t *hb = sH + (size_t)st * c.hstage;
           if (c.tma) {
             // one tensor copy: channels clo .. clo+nchm-1 of image n, each
@@ -561,9 +598,8 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
             const int xo = cg.ir0 * p.W, x0 = xo & ~3, ld = xo - x0;
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const int kl = lane + 32 * e;
-              roffs[st * 256 + (kl % kBWarps) * 32 + kl / kBWarps] =
-                  (kl < c.NR && rc[e] >= 0) ? rc[e] * c.PSw + ld + rt[e] : -1;
+              const int v = rb[e] + ld;
+              roffs[st * 256 + 32 * e + lane] = v >= 0 ? v : -1;
             }
             __syncwarp();
             if (lane == 0) {
@@ -586,11 +622,8 @@ tc_wgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
           __syncwarp();
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            // row kl goes to B-producer warp kl % 8, slot kl / 8 (entries past
-            // NR stay -1, read as zero rows)
-            const int kl = lane + 32 * e;
-            roffs[st * 256 + (kl % kBWarps) * 32 + kl / kBWarps] =
-                (kl < c.NR && rc[e] >= 0) ? rc[e] * c.PSw + lead[st * 64 + rc[e]] + rt[e] : -1;
+            // (entries past NR stay -1, read as zero rows)
+            roffs[st * 256 + 32 * e + lane] = rc[e] >= 0 ? rc[e] * c.PSw + lead[st * 64 + rc[e]] + rt[e] : -1;
           }
           __syncwarp();
           if (lane == 0) mbar_arrive_expect_tx(&h_full[st], bytes);
