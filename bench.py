@@ -59,16 +59,16 @@ L2_FLUSH_BYTES = 512 << 20
 STACK = "c5"
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
-# each main kernel on the c2 layer, from one ncu capture of those kernels
+# each main kernel on the c2 layer, from one ncu capture per kernel
 # (the command is in TRAFFIC_SOURCE).  Writes still in L2 when a kernel ends
 # are not counted by that capture.
 NCU_TRAFFIC_BYTES = {
-    ("c2", "forward"): 38.542336e6 + 13.854464e6,
-    ("c2", "dgrad"): 105.669376e6 + 16.545280e6,
-    ("c2", "wgrad"): 105.206016e6 + 14.017024e6,
+    ("c2", "forward"): 38.548480e6 + 14.362112e6,
+    ("c2", "dgrad"): 105.651456e6 + 16.430592e6,
+    ("c2", "wgrad"): 105.120000e6 + 14.597120e6,
 }
-TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:tc_(forward|dgrad|wgrad)_kernel -c 3 on the c2 layer "
-                  "(pc2d_forward + pc2d_backward of the seeded workload through the C ABI), not this run")
+TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:tc_<kernel>_kernel -c 1, one capture per kernel, of "
+                  "python bench.py --workload c2 --steps 1 --warmup 1 --no-stack --no-cpu-baseline (not this run)")
 
 # Kernel families the library can time (pc2d_timing_read).
 KERNELS = ("forward", "dgrad", "wgrad", "simt_forward", "simt_dgrad", "simt_wgrad")
