@@ -235,6 +235,7 @@ size_t pc2d_forward_workspace_size(int dtype, int n, int channels, int height, i
 int pc2d_forward(int dtype, const void *input, const void *pars, double factor, int k0, int k1, int s0, int s1,
                  int dl0, int dl1, int n, int channels, int height, int width, int m, void *output, void *hsum,
                  void *workspace, size_t workspace_bytes, void *stream) {
+  NvtxRange range("pc2d_forward");
   Problem p;
   int st = validate(dtype, n, channels, height, width, m, k0, k1, s0, s1, dl0, dl1, &p);
   if (st != PC2D_OK) return st;
@@ -335,6 +336,7 @@ int pc2d_backward(int dtype, const void *grad, const void *input, const void *pa
                   int k0, int k1, int s0, int s1, int dl0, int dl1, int n, int channels, int height, int width, int m,
                   int skip_input_grad, void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes,
                   void *stream) {
+  NvtxRange range("pc2d_backward");
   return backward_impl(dtype, grad, input, pars, hsum, factor, k0, k1, s0, s1, dl0, dl1, n, channels, height, width,
                        m, skip_input_grad, nullptr, false, inputgrad, parsgrad, workspace, workspace_bytes, stream);
 }
@@ -344,6 +346,7 @@ int pc2d_backward_interior(int dtype, const void *grad, const void *input, const
                            int height, int width, int m, int skip_input_grad, int pad_top, int pad_bottom,
                            int pad_left, int pad_right, double dx_scale, void *inputgrad, void *parsgrad,
                            void *workspace, size_t workspace_bytes, void *stream) {
+  NvtxRange range("pc2d_backward_interior");
   if (pad_top < 0 || pad_bottom < 0 || pad_left < 0 || pad_right < 0 || pad_top + pad_bottom > height ||
       pad_left + pad_right > width) {
     set_last_error("invalid padding %d/%d/%d/%d of a %dx%d input", pad_top, pad_bottom, pad_left, pad_right, height,
@@ -364,6 +367,7 @@ int pc2d_backward_interior(int dtype, const void *grad, const void *input, const
 
 int pc2d_pad_scale(int dtype, const void *input, int n, int channels, int height, int width, int pad_top,
                    int pad_bottom, int pad_left, int pad_right, double scale, void *output, void *stream) {
+  NvtxRange range("pc2d_pad_scale");
   if (dtype != PC2D_DTYPE_F32 && dtype != PC2D_DTYPE_F64) {
     set_last_error("unsupported dtype %d (float32 and float64 only)", dtype);
     return PC2D_ERR_INVALID_ARGUMENT;

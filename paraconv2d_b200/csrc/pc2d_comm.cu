@@ -239,6 +239,7 @@ int pc2d_backward_sum(pc2d_comm *c, int dtype, const void *grad, const void *inp
                       const void *hsum, double factor, int k0, int k1, int s0, int s1, int dl0, int dl1, int n,
                       int channels, int height, int width, int m, int skip_input_grad, void *inputgrad,
                       void *parsgrad, void *workspace, size_t workspace_bytes, void *stream) {
+  NvtxRange range("pc2d_backward_sum");
   if (!c || !c->connected) {
     set_last_error("pc2d_backward_sum: communicator not connected");
     return PC2D_ERR_INVALID_ARGUMENT;
@@ -276,6 +277,7 @@ int pc2d_backward_sum(pc2d_comm *c, int dtype, const void *grad, const void *inp
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // a programmatic dependent of the reduction that wrote the slot
+  NvtxRange sum_range("peer_sum");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(c->nblocks);
   cfg.blockDim = dim3(kSumThreads);

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include <mutex>
@@ -12,6 +13,17 @@
 #include "paraconv2d.h"
 
 namespace pc2d {
+
+// A named range on the profiler timeline for the duration of a scope (NVTX
+// push/pop; without an attached tool the calls return at once).  The C-ABI
+// entry points open one per call ("pc2d_forward", "pc2d_backward", ...) and
+// the backward one per kernel family it launches ("dgrad", "wgrad").
+struct NvtxRange {
+  explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange &) = delete;
+  NvtxRange &operator=(const NvtxRange &) = delete;
+};
 
 // Unique id (cuCtxGetId) of the CUDA context current on the calling thread;
 // 0 when no context is current or the driver cannot say.  Ids are never

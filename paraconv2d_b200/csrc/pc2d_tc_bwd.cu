@@ -739,10 +739,12 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
     dx_done = true;
   } else if (tc_dgcol_supported(p)) {
     // few input channels: dense GEMM over the output pixels + col2im
+    NvtxRange range("dgrad");
     const int st = tc_dgcol(p, grad, x, pars, hsum, dxo, dx, reinterpret_cast<char *>(ws) + wscr, stream);
     if (st != PC2D_OK) return st;
     dx_done = true;
   } else if (dg_supported(p)) {
+    NvtxRange range("dgrad");
     int *status = device_status_ptr();
     if (!status) {
       set_last_error("could not resolve the device status word");
@@ -773,6 +775,7 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
                                           /*leave_dx=*/false, /*skip_wgrad=*/true);
       if (st != PC2D_OK) return st;
     }
+    NvtxRange range("wgrad");
     if (nw) return nw_wgrad(p, grad, x, pars, hsum, factor, dpars, ws, stream);
     return tc_wgrad(p, grad, x, pars, hsum, factor, dpars, ws, stream);
   }

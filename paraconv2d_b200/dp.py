@@ -9,11 +9,18 @@ depend on the number of ranks.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from typing import Iterable, List, Optional
 
 import torch
 import torch.distributed as dist
+
+
+def _range(name: str, t: torch.Tensor):
+    """A named profiler range (NVTX) around host code that issues work for a
+    CUDA tensor; nothing for CPU tensors."""
+    return torch.cuda.nvtx.range(name) if t.is_cuda else contextlib.nullcontext()
 
 
 def shard_bounds(n: int, rank: int, world: int):
@@ -56,7 +63,8 @@ class GradAllReduce:
                 self._hooks.append(p.register_post_accumulate_grad_hook(self._on_grad))
 
     def _on_grad(self, p):
-        self._works.append(dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+        with _range("pc2d.allreduce.param", p.grad):
+            self._works.append(dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
 
     def __call__(self):
         """Call after backward: completes the sum of every gradient."""
@@ -77,7 +85,8 @@ class GradAllReduce:
             else:
                 seg.copy_(p.grad.reshape(-1))
             off += p.numel()
-        dist.all_reduce(self._flat, op=dist.ReduceOp.SUM, group=self.group)
+        with _range("pc2d.allreduce.bucket", self._flat):
+            dist.all_reduce(self._flat, op=dist.ReduceOp.SUM, group=self.group)
         off = 0
         for p in self.params:
             seg = self._flat[off:off + p.numel()].view_as(p)
