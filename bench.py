@@ -107,7 +107,8 @@ def parse_args():
     ap.add_argument("--stack-steps", type=int, default=20)
     ap.add_argument("--grad-sum", choices=["peer", "nccl"], default="peer",
                     help="N > 1: sum the parameter gradient inside the backward over NVLink peer memory "
-                         "(pc2d_backward_sum), or with an NCCL all-reduce after it")
+                         "(pc2d_backward_sum; the c5 step: one bucket by pc2d_comm_allreduce), or with NCCL "
+                         "all-reduces (after the backward; the c5 step: one per layer, overlapped)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU work of the baseline sample")
     return ap.parse_args()
 
@@ -583,7 +584,7 @@ def bench_stack(args, wl, lib, D, rank, world, steps):
     is accumulated, overlapping the backward of the layers below it."""
     import paraconv2d_b200 as pc
     from paraconv2d_b200 import _lib
-    from paraconv2d_b200.dp import GradAllReduce, shard
+    from paraconv2d_b200.dp import GradAllReduce, PeerGradComm, shard
 
     workloads = load_workloads()
     dev = D.dev
@@ -603,7 +604,17 @@ def bench_stack(args, wl, lib, D, rank, world, steps):
 
     model = make_model()
     params = list(model.parameters())
-    reducer = GradAllReduce(params, bucketed=False) if world > 1 else None
+    # the gradient sum over the ranks: one bucket summed over NVLink peer
+    # memory after the backward (--grad-sum peer), or one asynchronous NCCL
+    # all-reduce per layer from its post-accumulate-grad hook (--grad-sum nccl)
+    comm = None
+    reducer = None
+    if world > 1:
+        if args.grad_sum == "peer":
+            comm = PeerGradComm(sum(prm.numel() for prm in params))
+            reducer = GradAllReduce(params, bucketed=True, peer=comm)
+        else:
+            reducer = GradAllReduce(params, bucketed=False)
     xd = xs.to(dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -660,17 +671,25 @@ def bench_stack(args, wl, lib, D, rank, world, steps):
         e1.synchronize()
         e_tot += e0.elapsed_time(e1) / 1e3
     e_tot = D.max(e_tot)
-    # the all-reduce on its own: one flat bucket of all gradients, blocking
+    # the sum on its own: one flat bucket of all gradients, blocking, by the
+    # step's backend
     ar_ms = None
     if world > 1:
         flat = torch.cat([prm.grad.reshape(-1) for prm in params])
+
+        def flat_sum():
+            if comm is not None:
+                comm.allreduce_(flat)
+            else:
+                D.all_reduce(flat)
+
         for _ in range(3):
-            D.all_reduce(flat)
+            flat_sum()
         torch.cuda.synchronize()
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record(stream)
         for _ in range(steps):
-            D.all_reduce(flat)
+            flat_sum()
         a1.record(stream)
         a1.synchronize()
         ar_ms = D.max(a0.elapsed_time(a1) / steps)
@@ -701,8 +720,10 @@ def bench_stack(args, wl, lib, D, rank, world, steps):
     res = {
         "metric": metric_of(wl), "value": images / tot, "unit": UNIT, "n_gpus": world, "steps": steps,
         "ms_per_step": 1e3 * tot / steps, "scaling": "strong", "global_batch": wl.n, "per_gpu_batch": int(xs.shape[0]),
-        "allreduce": "one async NCCL all-reduce (SUM) per layer, issued from its post-accumulate-grad hook"
-                     if world > 1 else None,
+        "allreduce": (None if world == 1 else
+                      "one bucket of all layers' gradients summed over NVLink peer memory after the backward "
+                      "(pc2d_comm_allreduce)" if comm is not None else
+                      "one async NCCL all-reduce (SUM) per layer, issued from its post-accumulate-grad hook"),
         "allreduce_ms_flat_bucket": ar_ms,
         "e2e": {"value": images / e_tot, "unit": UNIT, "h2d_bytes_per_step": x_host.numel() * 4,
                 "d2h_bytes_per_step": sum(g.numel() * 4 for g in grads_host) + 4},
@@ -713,6 +734,8 @@ def bench_stack(args, wl, lib, D, rank, world, steps):
         res["tensor_frac_of_step"] = flops_img * wl.n / (tot / steps) / 1e12 / peak_3x / world
     if reducer is not None:
         reducer.remove()
+    if comm is not None:
+        comm.close()
     return res
 
 

@@ -177,7 +177,13 @@ int pc2d_backward_interior(int dtype, const void *grad, const void *input, const
  * on its communicator (like a collective); the calls of one communicator go
  * on one stream.  A rank that waits longer than 2 s for its peers records
  * PC2D_ERR_TIMEOUT in the device status (see above) and returns its own
- * gradient. */
+ * gradient.
+ * pc2d_comm_allreduce: dst = the sum over the ranks of every rank's src
+ * (count fp32 values, count <= max_params; dst may be src), the same bits on
+ * every rank, through the same exchange buffer: e.g. one bucket of several
+ * layers' parameter gradients after an autograd backward.  It shares the
+ * call sequence of pc2d_backward_sum (every rank the same calls, in the same
+ * order, on one stream) and its timeout behaviour (dst = own src). */
 typedef struct pc2d_comm pc2d_comm;
 size_t pc2d_comm_handle_bytes(void);
 int pc2d_comm_create(int rank, int world, size_t max_params, pc2d_comm **comm, void *handle_out);
@@ -187,6 +193,7 @@ int pc2d_backward_sum(pc2d_comm *comm, int dtype, const void *grad, const void *
                       const void *hsum, double factor, int k0, int k1, int s0, int s1, int dl0, int dl1,
                       int n, int channels, int height, int width, int m, int skip_input_grad,
                       void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes, void *stream);
+int pc2d_comm_allreduce(pc2d_comm *comm, const void *src, void *dst, size_t count, void *stream);
 
 /* Human-readable name of a pc2d_status. */
 const char *pc2d_status_string(int status);

@@ -70,8 +70,8 @@ __device__ __forceinline__ uint64_t now_ns() {
 // run-time rank would copy it to local memory.
 __global__ void __launch_bounds__(kSumThreads) peer_sum_kernel(PeerPtrs peers, int world, int rank, unsigned epoch,
                                                                int slot, int64_t stride, int64_t npars, int vpt,
-                                                               const unsigned *own_flags, float *__restrict__ out,
-                                                               int *status) {
+                                                               const unsigned *own_flags, const float *own_data,
+                                                               float *__restrict__ out, int *status) {
   __shared__ int s_ok;
   // the rank's own slice is written by the reduction this grid depends on
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -97,10 +97,17 @@ __global__ void __launch_bounds__(kSumThreads) peer_sum_kernel(PeerPtrs peers, i
     s_ok = ok;
   }
   __syncthreads();
-  if (!s_ok) return;
   const int64_t base = (int64_t)slot * stride;
   const int64_t nvec = (npars + 3) / 4;
   const int64_t v0 = (int64_t)blockIdx.x * kSumThreads * vpt;
+  if (!s_ok) {
+    // a peer did not arrive: the slice gets this rank's own values (the
+    // status word carries the error)
+    const float *own = own_data + base;
+    for (int64_t e = v0 * 4 + threadIdx.x; e < min(npars, (v0 + (int64_t)kSumThreads * vpt) * 4); e += kSumThreads)
+      out[e] = own[e];
+    return;
+  }
   for (int u = 0; u < vpt; ++u) {
     const int64_t v = v0 + (int64_t)u * kSumThreads + threadIdx.x;
     if (v >= nvec) break;
@@ -150,6 +157,37 @@ struct pc2d_comm {
 
 namespace {
 size_t flags_offset(size_t stride) { return align_up(2 * stride * sizeof(float), 256); }
+}  // namespace
+
+namespace {
+
+// The sum kernel over the first npars floats of every rank's slot, as a
+// programmatic dependent of whatever wrote this rank's slot last on the
+// stream (a kernel: its launch overlaps that kernel; a copy: plain order).
+int launch_peer_sum(pc2d_comm *c, unsigned epoch, int slot, int64_t npars, float *out, cudaStream_t s) {
+  int *status = device_status_ptr();
+  if (!status) {
+    set_last_error("could not resolve the device status word");
+    return PC2D_ERR_CUDA;
+  }
+  NvtxRange sum_range("peer_sum");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c->nblocks);
+  cfg.blockDim = dim3(kSumThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, peer_sum_kernel, c->ptrs, c->world, c->rank, epoch, slot,
+                                     (int64_t)c->stride, npars, c->vpt, (const unsigned *)c->ptrs.flags[c->rank],
+                                     (const float *)c->ptrs.data[c->rank], out, status));
+  PC2D_LAUNCH_CHECK("peer_sum_kernel");
+  c->epoch = epoch;
+  return PC2D_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -270,29 +308,41 @@ int pc2d_backward_sum(pc2d_comm *c, int dtype, const void *grad, const void *inp
                          m, skip_input_grad, inputgrad, mine, workspace, workspace_bytes, stream);
   if (st != PC2D_OK) return st;
   if (npars == 0) return PC2D_OK;
-  int *status = device_status_ptr();
-  if (!status) {
-    set_last_error("could not resolve the device status word");
-    return PC2D_ERR_CUDA;
+  return launch_peer_sum(c, epoch, slot, npars, static_cast<float *>(parsgrad),
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+int pc2d_comm_allreduce(pc2d_comm *c, const void *src, void *dst, size_t count, void *stream) {
+  NvtxRange range("pc2d_comm_allreduce");
+  if (!c || !c->connected) {
+    set_last_error("pc2d_comm_allreduce: communicator not connected");
+    return PC2D_ERR_INVALID_ARGUMENT;
   }
+  if (count > c->max_params || (count > 0 && (!src || !dst))) {
+    set_last_error("pc2d_comm_allreduce: %zu floats (the communicator holds %zu) or a null buffer", count,
+                   c->max_params);
+    return PC2D_ERR_INVALID_ARGUMENT;
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != c->dev) {
+    set_last_error("pc2d_comm_allreduce: the current device is not the communicator's (%d)", c->dev);
+    return PC2D_ERR_INVALID_ARGUMENT;
+  }
+  const int pend = pending_device_error();
+  if (pend != PC2D_OK) return pend;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // a programmatic dependent of the reduction that wrote the slot
-  NvtxRange sum_range("peer_sum");
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(c->nblocks);
-  cfg.blockDim = dim3(kSumThreads);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  PC2D_CUDA_CHECK(cudaLaunchKernelEx(&cfg, peer_sum_kernel, c->ptrs, c->world, c->rank, epoch, slot,
-                                     (int64_t)c->stride, npars, c->vpt, (const unsigned *)c->ptrs.flags[c->rank],
-                                     static_cast<float *>(parsgrad), status));
-  PC2D_LAUNCH_CHECK("peer_sum_kernel");
-  c->epoch = epoch;
-  return PC2D_OK;
+  if (count == 0) return PC2D_OK;
+  if (c->world == 1) {
+    if (src != dst) PC2D_CUDA_CHECK(cudaMemcpyAsync(dst, src, count * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    return PC2D_OK;
+  }
+  const unsigned epoch = c->epoch + 1;
+  const int slot = (int)(epoch & 1);
+  float *mine = c->ptrs.data[c->rank] + (size_t)slot * c->stride;
+  // this rank's values into its exchange slot, then the sum over the ranks
+  // (dst may be src: the sum reads the slots only)
+  PC2D_CUDA_CHECK(cudaMemcpyAsync(mine, src, count * sizeof(float), cudaMemcpyDeviceToDevice, s));
+  return launch_peer_sum(c, epoch, slot, (int64_t)count, static_cast<float *>(dst), s);
 }
 
 }  // extern "C"

@@ -48,13 +48,21 @@ class GradAllReduce:
     per parameter as soon as its gradient is accumulated, overlapping the
     backward of the layers below it; ``wait()`` completes them.  In that mode
     every parameter must receive a gradient on every rank in every step (the
-    ranks must issue the same collectives in the same order)."""
+    ranks must issue the same collectives in the same order).
+
+    ``peer`` (a ``PeerGradComm``, bucketed mode only) sums the bucket over
+    NVLink peer memory on the current stream instead of through NCCL: one
+    small kernel after the backward, where NCCL's all-reduce kernels would
+    wait for SMs that the layer kernels (one CTA per SM) hold."""
 
     def __init__(self, params: Iterable[torch.nn.Parameter], group: Optional[dist.ProcessGroup] = None,
-                 bucketed: bool = True):
+                 bucketed: bool = True, peer: Optional["PeerGradComm"] = None):
         self.params: List[torch.nn.Parameter] = [p for p in params if p.requires_grad]
         self.group = group
         self.bucketed = bucketed
+        if peer is not None and not bucketed:
+            raise ValueError("GradAllReduce: the peer sum works on the bucket (bucketed=True)")
+        self.peer = peer
         self._works = []
         self._hooks = []
         self._flat = None
@@ -85,8 +93,11 @@ class GradAllReduce:
             else:
                 seg.copy_(p.grad.reshape(-1))
             off += p.numel()
-        with _range("pc2d.allreduce.bucket", self._flat):
-            dist.all_reduce(self._flat, op=dist.ReduceOp.SUM, group=self.group)
+        if self.peer is not None:
+            self.peer.allreduce_(self._flat)
+        else:
+            with _range("pc2d.allreduce.bucket", self._flat):
+                dist.all_reduce(self._flat, op=dist.ReduceOp.SUM, group=self.group)
         off = 0
         for p in self.params:
             seg = self._flat[off:off + p.numel()].view_as(p)
@@ -143,6 +154,21 @@ class PeerGradComm:
         st = self._lib.pc2d_comm_connect(self.comm, blob)
         if st != 0:
             raise RuntimeError(status_message(st))
+
+    def allreduce_(self, t: torch.Tensor) -> torch.Tensor:
+        """In place: t = the sum over the ranks of every rank's t (fp32,
+        contiguous, on this rank's GPU, at most ``max_params`` values), on the
+        current stream, the same bits on every rank.  Collective: every rank
+        calls it in the same order."""
+        from ._lib import status_message
+
+        if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("PeerGradComm.allreduce_: a contiguous float32 CUDA tensor")
+        st = self._lib.pc2d_comm_allreduce(self.comm, t.data_ptr(), t.data_ptr(), t.numel(),
+                                           torch.cuda.current_stream(t.device).cuda_stream)
+        if st != 0:
+            raise RuntimeError(status_message(st))
+        return t
 
     def close(self):
         if self.comm is not None:

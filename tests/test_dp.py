@@ -121,3 +121,13 @@ def test_bucket_spans_parameters_without_gradient():
     mp.start_processes(_worker_missing, args=(2, _free_port(), out), nprocs=2, join=True, start_method="spawn")
     for r in range(2):
         assert torch.allclose(out[r], ref, rtol=1e-12, atol=1e-12)
+
+
+def test_peer_sum_needs_the_bucketed_mode():
+    """The NVLink peer sum works on the flat bucket only: asking for it with
+    per-parameter all-reduces is refused before any hook is registered."""
+    from paraconv2d_b200.dp import GradAllReduce
+
+    p = torch.nn.Parameter(torch.zeros(4))
+    with pytest.raises(ValueError):
+        GradAllReduce([p], bucketed=False, peer=object())

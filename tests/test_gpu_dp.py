@@ -1,10 +1,11 @@
 """Data-parallel gradient of the c5 stack through the CUDA kernels: two ranks,
-each with its shard of the batch, sum their parameter gradients with one
-all-reduce; the result must equal the gradient of the whole batch computed
-in one process (max|a-b| <= 1e-4 max|b| per layer: the two differ only in
-the order of the fp32 sums).  Both all-reduce modes of GradAllReduce are
-checked: one bucket after the backward, and one asynchronous all-reduce per
-layer issued as soon as that layer's gradient is accumulated.
+each with its shard of the batch, sum their parameter gradients; the result
+must equal the gradient of the whole batch computed in one process
+(max|a-b| <= 1e-4 max|b| per layer: the two differ only in the order of the
+fp32 sums).  Three modes of GradAllReduce are checked: one NCCL bucket after
+the backward, one asynchronous NCCL all-reduce per layer issued as soon as
+that layer's gradient is accumulated, and (two GPUs) one bucket summed over
+NVLink peer memory (pc2d_comm_allreduce).
 
 The ranks use NCCL with one GPU each when two GPUs are visible, else gloo
 with both ranks on GPU 0 (no kernel of one rank waits for the other's; the
@@ -49,11 +50,11 @@ def _grads(model):
     return torch.cat([p.grad.reshape(-1) for p in model.parameters()]).cpu()
 
 
-def _worker(rank, world, port, bucketed, outdir):
+def _worker(rank, world, port, mode, outdir):
     import torch.distributed as dist
 
     from paraconv2d_b200 import workloads
-    from paraconv2d_b200.dp import GradAllReduce, shard
+    from paraconv2d_b200.dp import GradAllReduce, PeerGradComm, shard
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -65,13 +66,20 @@ def _worker(rank, world, port, bucketed, outdir):
     dist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60), **kw)
     try:
         model = _model(dev)
-        red = GradAllReduce(model.parameters(), bucketed=bucketed)
+        comm = None
+        if mode == "peer_bucket":
+            comm = PeerGradComm(sum(p.numel() for p in model.parameters()))
+            red = GradAllReduce(model.parameters(), bucketed=True, peer=comm)
+        else:
+            red = GradAllReduce(model.parameters(), bucketed=(mode == "one_bucket"))
         x = shard(_batch(), rank, world).to(dev)
         workloads.stack_loss(model(x)).backward()
         red()
         torch.cuda.synchronize()
         torch.save(_grads(model), os.path.join(outdir, f"rank{rank}.pt"))
         red.remove()
+        if comm is not None:
+            comm.close()
     finally:
         dist.destroy_process_group()
 
@@ -84,8 +92,8 @@ def _free_port():
     return port
 
 
-@pytest.mark.parametrize("bucketed", [True, False], ids=["one_bucket", "per_layer_overlapped"])
-def test_two_rank_gradient_equals_full_batch(bucketed, tmp_path):
+@pytest.mark.parametrize("mode", ["one_bucket", "per_layer_overlapped", "peer_bucket"])
+def test_two_rank_gradient_equals_full_batch(mode, tmp_path):
     from paraconv2d_b200 import workloads
     from pc2d_testutil import maxrel_excess
 
@@ -93,7 +101,9 @@ def test_two_rank_gradient_equals_full_batch(bucketed, tmp_path):
     model = _model(dev)
     workloads.stack_loss(model(_batch().to(dev))).backward()
     ref = [p.grad.detach().cpu().clone() for p in model.parameters()]
-    mp.start_processes(_worker, args=(2, _free_port(), bucketed, str(tmp_path)), nprocs=2, join=True,
+    if mode == "peer_bucket" and torch.cuda.device_count() < 2:
+        pytest.skip("the peer sum needs two GPUs")
+    mp.start_processes(_worker, args=(2, _free_port(), mode, str(tmp_path)), nprocs=2, join=True,
                        start_method="spawn")
     for r in range(2):
         got = torch.load(os.path.join(tmp_path, f"rank{r}.pt"))
@@ -162,3 +172,45 @@ def test_peer_sum_equals_nccl_allreduce(tmp_path):
     r1 = torch.load(os.path.join(tmp_path, "peer1.pt"))
     assert all(a and b for a, b in r0["results"] + r1["results"])
     assert torch.equal(r0["dp"], r1["dp"])
+
+
+def _allreduce_worker(rank, world, port, outdir):
+    import torch.distributed as dist
+
+    from paraconv2d_b200.dp import PeerGradComm
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        comm = PeerGradComm(186_496)
+        results = []
+        for count in (1001, 186_496, 3):  # both exchange slots, a ragged tail, the full bucket
+            gen = torch.Generator().manual_seed(1000 * count + rank)
+            t = (torch.randn(count, generator=gen) * 1e-3).to(dev)
+            ref = t.clone()
+            dist.all_reduce(ref)
+            comm.allreduce_(t)
+            torch.cuda.synchronize()
+            results.append(torch.equal(t, ref))
+        from paraconv2d_b200 import _lib
+        assert _lib.cabi().pc2d_device_status() == 0
+        comm.close()
+        torch.save({"results": results, "last": t.cpu()}, os.path.join(outdir, f"ar{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_allreduce_equals_nccl(tmp_path):
+    """pc2d_comm_allreduce on two GPUs: in place, counts that are and are not
+    multiples of four, equal to NCCL's all-reduce bit for bit on both ranks."""
+    mp.start_processes(_allreduce_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    r0 = torch.load(os.path.join(tmp_path, "ar0.pt"))
+    r1 = torch.load(os.path.join(tmp_path, "ar1.pt"))
+    assert all(r0["results"]) and all(r1["results"])
+    assert torch.equal(r0["last"], r1["last"])
