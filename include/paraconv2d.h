@@ -195,6 +195,22 @@ int pc2d_backward_sum(pc2d_comm *comm, int dtype, const void *grad, const void *
                       void *inputgrad, void *parsgrad, void *workspace, size_t workspace_bytes, void *stream);
 int pc2d_comm_allreduce(pc2d_comm *comm, const void *src, void *dst, size_t count, void *stream);
 
+/* ---------------------------------------------------------------------------
+ * Optimizer step on one layer's flat parameter vector [h0 | h | p | p0]
+ * (m output channels, window of d = C*k0*k1 elements), using the multipliers
+ * the module attaches to `pars` (reference ptparaconv2d.py:194-198):
+ *   d_i   = grad_i + (weight_decay * wd_factor) * w_i
+ *   buf_i = momentum * buf_i + d_i     (buf_i = d_i when first_step != 0;
+ *                                       momentum_buf unused when momentum == 0)
+ *   w_i  -= (lr * factor_i) * buf_i,   factor = h_lr_factor on [h0 | h] (the
+ *                                       first m*(1+d) values), p_lr_factor on [p | p0]
+ * i.e. torch.optim.SGD (no dampening, no Nesterov) with the learning rate and
+ * weight decay scaled per parameter group, in one pass over HBM.  dtype F32 or
+ * F64; pars, grad and momentum_buf hold 2*m*(1+d) values each. */
+int pc2d_param_step(int dtype, void *pars, const void *grad, void *momentum_buf, int m, int d, double lr,
+                    double h_lr_factor, double p_lr_factor, double weight_decay, double wd_factor,
+                    double momentum, int first_step, void *stream);
+
 /* Human-readable name of a pc2d_status. */
 const char *pc2d_status_string(int status);
 

@@ -86,6 +86,7 @@ def cabi() -> ctypes.CDLL:
             "pc2d_comm_destroy": ([P], I),
             "pc2d_backward_sum": ([P, I, P, P, P, P, D] + [I] * 12 + [P, P, P, S, P], I),
             "pc2d_comm_allreduce": ([P, P, P, S, P], I),
+            "pc2d_param_step": ([I, P, P, P, I, I] + [D] * 6 + [I, P], I),
             "pc2d_status_string": ([I], ctypes.c_char_p),
             "pc2d_last_error": ([], ctypes.c_char_p),
             "pc2d_device_status": ([], I),
