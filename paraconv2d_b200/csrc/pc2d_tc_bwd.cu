@@ -74,7 +74,8 @@ struct DgCfg {
   int nJB;          // j-blocks
   int nK;           // weight stages of the prep layout = nJB * T
   int nph;          // stride phases (y mod s0, x mod s1)
-  int ph_rows[kMaxPh], ph_cols[kMaxPh];   // phase grid of an image
+  int ph_rows[kMaxPh], ph_cols[kMaxPh];   // phase grid of an image's pixel window
+  int ph_a0[kMaxPh], ph_b0[kMaxPh];       // its first row and column within the phase's full grid
   int ph_ntaps[kMaxPh];                   // taps that reach the phase
   int ph_first[kMaxPh + 1];               // first tile of each phase within an image
   int ph_tap0[kMaxPh + 1];                // first entry of each phase in the tap table
@@ -94,8 +95,21 @@ struct DgPhases {
   int tap0[kMaxPh + 1];
   int rows[kMaxPh];
   int cols[kMaxPh];
+  int a0[kMaxPh];
+  int b0[kMaxPh];
   int ntaps[kMaxPh];
 };
+
+// The input pixels whose gradient is computed: rows [y0, y1) and columns
+// [x0, x1) of the padded input.  The op needs all of them; a module that pads
+// its input needs only the unpadded interior, and tiling just that saves the
+// tiles of the border (on a 34x34 padded plane 8 tiles of 128 pixels instead
+// of 10; on a stride-2 layer's 17x17 phase grids 2 instead of 3).
+struct DgWindow {
+  int y0, y1, x0, x1;
+};
+
+inline DgWindow dg_full_window(const Problem &p) { return DgWindow{0, p.H, 0, p.W}; }
 
 // Taps that reach input rows y with y % s0 == py: tap row (k0-1-ix2)*dl0 must
 // have the same residue (the output pixel is then (y - row)/s0 exactly).
@@ -109,7 +123,10 @@ inline int phase_rows(int k, int dl, int s, int py, int *list) {
   return n;
 }
 
-DgCfg dg_cfg(const Problem &p) {
+// First index i >= 0 of the progression r + s*i that is >= v.
+inline int first_at_or_after(int v, int r, int s) { return v > r ? (v - r + s - 1) / s : 0; }
+
+DgCfg dg_cfg(const Problem &p, const DgWindow &w) {
   DgCfg c;
   c.ncb = std::max(1, ceil_div(p.C, kMaxNC));
   const int nc = ceil_div(p.C, c.ncb);
@@ -121,14 +138,17 @@ DgCfg dg_cfg(const Problem &p) {
   c.tpi = 0;
   for (int ph = 0; ph < kMaxPh; ++ph) {
     c.ph_rows[ph] = c.ph_cols[ph] = c.ph_ntaps[ph] = 0;
+    c.ph_a0[ph] = c.ph_b0[ph] = 0;
     c.ph_first[ph] = 0;
     c.ph_tap0[ph] = 0;
   }
   int taps = 0;
   for (int ph = 0; ph < c.nph && ph < kMaxPh; ++ph) {
     const int py = ph / p.s1, px = ph % p.s1;
-    c.ph_rows[ph] = p.H > py ? (p.H - py + p.s0 - 1) / p.s0 : 0;
-    c.ph_cols[ph] = p.W > px ? (p.W - px + p.s1 - 1) / p.s1 : 0;
+    c.ph_a0[ph] = first_at_or_after(w.y0, py, p.s0);
+    c.ph_b0[ph] = first_at_or_after(w.x0, px, p.s1);
+    c.ph_rows[ph] = std::max(0, first_at_or_after(w.y1, py, p.s0) - c.ph_a0[ph]);
+    c.ph_cols[ph] = std::max(0, first_at_or_after(w.x1, px, p.s1) - c.ph_b0[ph]);
     c.ph_ntaps[ph] = phase_rows(p.k0, p.dl0, p.s0, py, nullptr) * phase_rows(p.k1, p.dl1, p.s1, px, nullptr);
     c.ph_first[ph] = c.tpi;
     c.ph_tap0[ph] = taps;
@@ -196,6 +216,7 @@ struct DgGeo {
   int ph, py, px;  // stride phase
   int q0;          // first phase-grid pixel of the tile
   int cols, npix;  // phase grid width and size
+  int a0, b0;      // first row and column of the phase grid (within the phase's full grid)
   int oylo;        // first output row staged
   int orows;       // output rows staged (may be 0)
   int ntaps;       // taps reaching this phase
@@ -214,10 +235,12 @@ __device__ __forceinline__ DgGeo dg_geo(const Problem &p, const DgCfg &c, const 
   g.q0 = (r - ps.first[ph]) * kTileM;
   g.cols = ps.cols[ph];
   g.npix = ps.rows[ph] * g.cols;
+  g.a0 = ps.a0[ph];
+  g.b0 = ps.b0[ph];
   g.ntaps = ps.ntaps[ph];
   g.tap0 = ps.tap0[ph];
   const int qlast = min(g.q0 + kTileM - 1, g.npix - 1);
-  const int ya = g.py + p.s0 * (g.q0 / g.cols), yb = g.py + p.s0 * (qlast / g.cols);
+  const int ya = g.py + p.s0 * (g.a0 + g.q0 / g.cols), yb = g.py + p.s0 * (g.a0 + qlast / g.cols);
   const int lo = ya - (p.k0 - 1) * p.dl0;
   const int oylo = lo <= 0 ? 0 : (lo + p.s0 - 1) / p.s0;
   const int oyhi = min(p.P - 1, yb / p.s0);
@@ -300,6 +323,8 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
     for (int i = 0; i < kMaxPh; ++i) {
       ps.rows[i] = c.ph_rows[i];
       ps.cols[i] = c.ph_cols[i];
+      ps.a0[i] = c.ph_a0[i];
+      ps.b0[i] = c.ph_b0[i];
       ps.ntaps[i] = c.ph_ntaps[i];
     }
   }
@@ -350,7 +375,8 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       const DgGeo tg = dg_geo(p, c, ps, item / c.ncb);
       const int q = tg.q0 + r;
       const bool pvalid = q < tg.npix;
-      const int ay = q / tg.cols, bx = q - ay * tg.cols;  // phase-grid position
+      const int qa = q / tg.cols;
+      const int ay = tg.a0 + qa, bx = tg.b0 + (q - qa * tg.cols);  // phase-grid position
       float sg = 0.f;
       for (int jb = 0; jb < c.nJB && ok; ++jb, ++jit) {
         const uint32_t js = jit & 1, jph = (jit >> 1) & 1;
@@ -436,8 +462,8 @@ tc_dgrad_kernel(const float *__restrict__ grad, const float *__restrict__ x, con
       const bool pv = q < tg.npix;
       int64_t xb = 0, ob = -1;
       if (pv) {
-        const int ay = q / tg.cols;
-        const int yy = tg.py + p.s0 * ay, xx = tg.px + p.s1 * (q - ay * tg.cols);
+        const int qa = q / tg.cols;
+        const int yy = tg.py + p.s0 * (tg.a0 + qa), xx = tg.px + p.s1 * (tg.b0 + q - qa * tg.cols);
         xb = tg.n * p.CHW + (int64_t)yy * p.W + xx;
         ob = dx_index(dxo, tg.n, yy, xx);
 #pragma unroll 8
@@ -698,11 +724,12 @@ int launch_dgrad(const Problem &p, DgCfg c, const float *grad, const float *x, c
   return PC2D_OK;
 }
 
+bool dg_cfg_fits(const DgCfg &c) { return dg_smem_bytes(c) <= (size_t)kSmemLimit && c.PSo * 2 * kJB < (1 << 30); }
+
 bool dg_supported(const Problem &p) {
   if (p.NPQ <= 0 || p.m < 1 || p.HW >= ((int64_t)1 << 30) || p.PQ >= ((int64_t)1 << 30)) return false;
   if (p.s0 * p.s1 > kMaxPh || p.k0 > kMaxKs || p.k1 > kMaxKs) return false;
-  const DgCfg c = dg_cfg(p);
-  return dg_smem_bytes(c) <= (size_t)kSmemLimit && c.PSo * 2 * kJB < (1 << 30);
+  return dg_cfg_fits(dg_cfg(p, dg_full_window(p)));
 }
 
 }  // namespace
@@ -724,7 +751,7 @@ size_t tc_backward_workspace(const Problem &p, bool skip_input_grad) {
   size_t ws = wgrad_scratch(p, skip_input_grad);
   if (!skip_input_grad) {
     if (tc_dgcol_supported(p)) ws += align_up(tc_dgcol_workspace(p), 256);
-    else if (dg_supported(p)) ws += align_up(dg_bsplit_bytes(dg_cfg(p)), 256);
+    else if (dg_supported(p)) ws += align_up(dg_bsplit_bytes(dg_cfg(p, dg_full_window(p))), 256);
   }
   return ws;
 }
@@ -750,12 +777,21 @@ int tc_backward(const Problem &p, const float *grad, const float *x, const float
       set_last_error("could not resolve the device status word");
       return PC2D_ERR_CUDA;
     }
-    const DgCfg c = dg_cfg(p);
+    // only the pixels whose gradient is written are tiled (the interior, for
+    // a module that pads its input), unless that geometry needs more shared
+    // memory than the whole plane's
+    DgCfg c = dg_cfg(p, dg_full_window(p));
+    if (dxo.Hu < p.H || dxo.Wu < p.W) {
+      const DgCfg ci = dg_cfg(p, DgWindow{dxo.pt, dxo.pt + dxo.Hu, dxo.pl, dxo.pl + dxo.Wu});
+      if (dg_cfg_fits(ci)) c = ci;
+    }
     float *wsB = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + wscr);
     tc_dg_prep_weights<<<dim3(c.nK, c.ncb, c.NC / 8), 256, 0, stream>>>(pars, p, c, wsB);
     PC2D_LAUNCH_CHECK("tc_dg_prep_weights");
     int st = PC2D_OK;
+    if (c.items == 0) c.NC = 0;  // an empty interior: nothing to launch
     switch (c.NC) {
+      case 0: break;
       case 16: st = launch_dgrad<16>(p, c, grad, x, hsum, wsB, dxo, dx, status, stream); break;
       case 32: st = launch_dgrad<32>(p, c, grad, x, hsum, wsB, dxo, dx, status, stream); break;
       case 48: st = launch_dgrad<48>(p, c, grad, x, hsum, wsB, dxo, dx, status, stream); break;
