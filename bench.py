@@ -499,9 +499,15 @@ def bench_layer(args, wl, lib, D, rank, world):
     x_slots = [torch.empty(x.shape, device=dev) for _ in range(2)]
     g_slots = [torch.empty(grad.shape, device=dev) for _ in range(2)]
     slot_free = [None, None]
+    slot_out = [None, None]
 
     def e2e_step(i):
         s = i % 2
+        # at most two steps in flight, as with a loader's bounded queue: the
+        # host waits for step i-2's results before it queues step i (an
+        # unbounded run-ahead would grow the allocator's pool step by step)
+        if slot_out[s] is not None:
+            slot_out[s].synchronize()
         with torch.cuda.stream(h2d_stream):
             if slot_free[s] is not None:
                 h2d_stream.wait_event(slot_free[s])
@@ -529,6 +535,9 @@ def bench_layer(args, wl, lib, D, rank, world):
             d2h_stream.wait_event(done)
             dx_host.copy_(dxv, non_blocking=True)
             dp_host.copy_(dpv, non_blocking=True)
+            out_done = torch.cuda.Event()
+            out_done.record(d2h_stream)
+        slot_out[s] = out_done
 
     def e2e_run(steps, start_event=None, end_event=None):
         if start_event is not None:
