@@ -629,9 +629,11 @@ def bench_stack(args, wl, lib, D, rank, world, steps):
     """Data-parallel training step of the layer stack (the c5 workload:
     3->32->64->64->64, k3 p1, stride 2 on layers 2-3, 64x64 input, global
     batch 1024, loss sum((2^-40 out)^2)).  The global batch is split across
-    the ranks (strong scaling); each layer's parameter gradient is summed
-    across the ranks by an asynchronous NCCL all-reduce issued as soon as it
-    is accumulated, overlapping the backward of the layers below it."""
+    the ranks (strong scaling); the parameter gradients are summed across
+    the ranks: one bucket of all layers' gradients over NVLink peer memory
+    after the backward (--grad-sum peer, the default), or one asynchronous
+    NCCL all-reduce per layer issued as soon as its gradient is accumulated
+    (--grad-sum nccl)."""
     import paraconv2d_b200 as pc
     from paraconv2d_b200 import _lib
     from paraconv2d_b200.dp import GradAllReduce, PeerGradComm, shard

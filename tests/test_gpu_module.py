@@ -181,6 +181,26 @@ def test_other_padding_modes_take_the_reference_route():
     assert elementwise_excess(y.detach().cpu().numpy(), out) <= 1.0
 
 
+@pytest.mark.parametrize("shape,pads", [((3, 5, 64, 64), (1, 1, 1, 1)), ((64, 32, 64, 64), (1, 1, 1, 1)),
+                                        ((7, 3, 16, 16), (1, 1, 1, 1)), ((1, 2, 7, 100), (0, 0, 5, 0)),
+                                        ((2, 2, 3, 3), (2, 2, 2, 2)), ((5, 1, 1, 1), (0, 0, 0, 0))])
+def test_cabi_pad_scale_shapes(shape, pads):
+    """pc2d_pad_scale equals F.pad(scale * x) bitwise on wide and narrow rows
+    (segments of several padded rows, planes crossing segments, rows shorter
+    than a warp), including a c5 layer's 64x64 planes."""
+    from paraconv2d_b200 import _lib
+
+    lib = _lib.cabi()
+    n, C, H, W = shape
+    pt, pb, pl, pr = pads
+    torch.manual_seed(3)
+    x = (torch.rand(n, C, H, W) * 2 - 1).cuda()
+    xp = torch.full((n, C, H + pt + pb, W + pl + pr), float("nan"), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.pc2d_pad_scale(0, x.data_ptr(), n, C, H, W, pt, pb, pl, pr, 0.75, xp.data_ptr(), stream) == 0
+    assert torch.equal(xp, F.pad(0.75 * x, (pl, pr, pt, pb)))
+
+
 @pytest.mark.parametrize("dtype,code", [(torch.float32, 0), (torch.float64, 1)])
 def test_cabi_pad_scale_and_interior_backward(dtype, code):
     """pc2d_pad_scale equals F.pad(scale * x) bitwise; pc2d_backward_interior
