@@ -76,7 +76,15 @@ int pad_scale(int dtype, const void *in, int n, int C, int H, int W, int pt, int
   const int R = std::max(1, kPadSegment / Wp);
   const int64_t segments = (rows + R - 1) / R;
   const int64_t want = (segments + kPadThreads / 32 - 1) / (kPadThreads / 32);
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * 8));
+  // one resident wave: the warps loop over the segments, so a second,
+  // partial wave of blocks would run as long as the first
+  int per_sm = 0;
+  if (dtype == PC2D_DTYPE_F32)
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pad_scale_kernel<float>, kPadThreads, 0);
+  else
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pad_scale_kernel<double>, kPadThreads, 0);
+  per_sm = std::max(1, per_sm);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * per_sm));
   if (dtype == PC2D_DTYPE_F32)
     pad_scale_kernel<float><<<grid, kPadThreads, 0, stream>>>((const float *)in, rows, Hp, Wp, H, W, pt, pl, R,
                                                               (float)scale, (float *)out);
