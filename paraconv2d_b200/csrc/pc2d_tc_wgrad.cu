@@ -25,7 +25,7 @@
 //   - the MMA thread issues Ahi*Bhi + Alo*Bhi + Ahi*Blo (N = NR) per 8
 //     pixels.
 // At the end of a segment the epilogue warps drain the fp32 accumulator to a
-// per-segment slice of the workspace (a partial over at most 4096 pixels, so
+// per-segment slice of the workspace (a partial over at most 2048 pixels, so
 // the tensor core's per-instruction accumulation error stays small; a longer
 // segment also halves the slices the reduction reads); a second
 // kernel sums the slices in a fixed order in fp64 and applies the epilogue
@@ -53,7 +53,7 @@ using tc::warp_wait;
 constexpr int kChunk = 32;        // pixels per K chunk
 constexpr int kAhead = 8;         // chunks an A producer prefetches ahead (L2)
 constexpr int kStages = 3;
-constexpr int kMaxSeg = 128;      // chunks per segment
+constexpr int kMaxSeg = 64;       // chunks per segment
 constexpr int kThreads = 608;
 constexpr int kBWarps = 8;
 constexpr int kMinSmem = 120 * 1024;
